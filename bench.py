@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""Benchmark driver: FP16 GEMM TFLOP/s on B200, one JSON line.
+
+Default workload (N=1): configuration 2 of the reference's baseline, the
+4096^3 fp16 GEMM with fused BiasGeLU (tanh) epilogue and fp16 output, on
+synthetic seeded inputs resident in HBM.  A step is one launch of the GEMM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config 1..5]
+                  [--impl pax|reference] [--gather]
+
+With N > 1 (launched under torchrun, one rank per GPU) the GEMM is split
+along N: rank p owns the column slab [p*Ns, (p+1)*Ns) of B, bias and C with
+Ns = N of the configuration (weak scaling: per-GPU work is fixed), and
+--gather adds an NCCL all-gather of the C slabs into a replicated C.
+`value` = total FLOPs of all ranks / max-over-ranks device time.
+
+--impl reference times the reference's own CPU GEMM (cpu_gemm_ref of
+src/host_bridge.c, compiled from its sources into oracle/_ref) on all host
+cores over a bounded row sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "FP16 GEMM TFLOP/s & % of B200 dense peak (4096³ BiasGeLU); 1/2/4/8-GPU scaling"
+CONFIGS = {
+    1: dict(M=1024, N=1024, K=1024, epi="none", dist="uniform", name="C1: 1024^3 fp16 GEMM, no epilogue"),
+    2: dict(M=4096, N=4096, K=4096, epi="bias_gelu_tanh", dist="uniform",
+            name="C2: 4096^3 fp16 GEMM + BiasGeLU(tanh), fp16 out"),
+    3: dict(M=16384, N=16384, K=4096, epi="residual_gelu_erf", dist="normal",
+            name="C3: M16384 K4096 N16384 + ResidualGeLU(erf), fp16 out"),
+    4: dict(M=16, N=16384, K=4096, epi="bias", dist="normal", name="C4: M16 K4096 N16384 + Bias, fp16 out"),
+    5: dict(M=32768, N=32768, K=32768, epi="bias_gelu_tanh", dist="uniform",
+            name="C5: 32768^3 fp16 GEMM + BiasGeLU(tanh), fp16 out"),
+}
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="pax", choices=["pax", "reference"])
+    ap.add_argument("--gather", action="store_true")
+    ap.add_argument("--seed", type=int, default=0x5EED)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    return ap.parse_args()
+
+
+def rank_env():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(
+        os.environ.get("LOCAL_RANK", "0"))
+
+
+# ------------------------------------------------------------------ CPU legs
+def cpu_reference_lib():
+    """(callable(A,B,C,m,n,k), kind): the reference build if present, else the port."""
+    import oracle
+
+    L = oracle.ref_lib()
+    if L is not None:
+        return L.paxref_cpu_gemm_ref, "reference"
+    O = oracle.lib()
+    return O.oracle_cpu_gemm_ref, "port"
+
+
+def cpu_gemm_sample(cfg, seconds: float, seed: int, threads: int | None = None):
+    """Time cpu_gemm_ref on a row sample of the workload using all host cores.
+
+    Rows are split into blocks, one ctypes call per block (the GIL is released
+    during the call).  Returns (TFLOP/s, seconds, rows, threads, kind, flops).
+    """
+    import numpy as np
+
+    fn, kind = cpu_reference_lib()
+    M, N, K = cfg["M"], cfg["N"], cfg["K"]
+    rng = np.random.default_rng(seed)
+    B = rng.uniform(-1, 1, (K, N)).astype(np.float16).astype(np.float32)
+    threads = threads or os.cpu_count() or 1
+    # calibrate on one row
+    a1 = rng.uniform(-1, 1, (1, K)).astype(np.float16).astype(np.float32)
+    c1 = np.empty((1, N), np.float32)
+    t0 = time.perf_counter()
+    fn(a1.ctypes.data, B.ctypes.data, c1.ctypes.data, 1, N, K)
+    t_row = max(time.perf_counter() - t0, 1e-6)
+    rows = int(max(threads, min(M, seconds * threads / t_row)))
+    rows = max(threads, (rows // threads) * threads)
+    rows = min(rows, M) if M >= threads else M
+    A = rng.uniform(-1, 1, (rows, K)).astype(np.float16).astype(np.float32)
+    C = np.empty((rows, N), np.float32)
+    per = (rows + threads - 1) // threads
+    blocks = [(r0, min(per, rows - r0)) for r0 in range(0, rows, per)]
+
+    def work(b):
+        r0, nr = b
+        fn(A[r0:].ctypes.data, B.ctypes.data, C[r0:].ctypes.data, nr, N, K)
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=len(blocks)) as ex:
+        list(ex.map(work, blocks))
+    dt = time.perf_counter() - t0
+    flops = 2.0 * rows * N * K
+    return flops / dt / 1e12, dt, rows, len(blocks), kind, flops
+
+
+def run_reference(args):
+    rank, world, _ = rank_env()
+    if rank != 0:
+        return 0
+    cfg = CONFIGS[args.config]
+    per_step = max(2.0, min(args.cpu_seconds, 150.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_gemm_sample(cfg, per_step, args.seed)
+    vals, secs = [], []
+    rows = threads = 0
+    kind = ""
+    for i in range(args.steps):
+        v, dt, rows, threads, kind, _ = cpu_gemm_sample(cfg, per_step, args.seed + i)
+        vals.append(v)
+        secs.append(dt)
+    value = statistics.mean(vals)
+    sample = (f"{rows} of {cfg['M']} rows of {cfg['name']} per step (cpu_gemm_ref i-j-l fp32 loop, fp32 inputs "
+              f"widened from fp16), {threads} row blocks in parallel")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1e3 * statistics.mean(secs),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded uniform[-1,1] fp16 widened to fp32)",
+        "config": workload_config(cfg, world, args),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(cfg, world, args):
+    return {
+        "workload": cfg["name"],
+        "M": cfg["M"],
+        "N_per_gpu": cfg["N"],
+        "N_total": cfg["N"] * world,
+        "K": cfg["K"],
+        "epilogue": cfg["epi"],
+        "inputs": cfg["dist"],
+        "parallelism": f"N-split over {world} GPU(s)" + (" + NCCL all-gather of C" if args.gather else ""),
+        "l2": "flushed between steps (256 MiB write)",
+    }
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (the recipe's clocks line)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, pw, reasons = [], 0.0, [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+                pw.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        loaded = [s for s, p in zip(sm, pw) if p >= 0.5 * max(pw)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(pw)}
+
+
+# ------------------------------------------------------------------ GPU leg
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 6650.0, "fallback"
+
+
+def traffic_from_profiles(config: int):
+    """DRAM bytes per launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"traffic_c{config}.txt")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+def run_pax(args):
+    import numpy as np  # noqa: F401
+    import torch
+    import torch.distributed as dist
+
+    import pax_b200
+
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    cfg = CONFIGS[args.config]
+    M, N, K = cfg["M"], cfg["N"], cfg["K"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 1000 * rank)
+    if cfg["dist"] == "uniform":
+        A = (torch.rand((M, K), generator=g, device=dev) * 2 - 1).half()
+        B = (torch.rand((K, N), generator=g, device=dev) * 2 - 1).half()
+    else:
+        A = torch.randn((M, K), generator=g, device=dev).half()
+        B = (torch.randn((K, N), generator=g, device=dev) * 0.02).half()
+    bias = torch.randn((N,), generator=g, device=dev).half()
+    res = torch.randn((M, N), generator=g, device=dev).half() if "residual" in cfg["epi"] else None
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    gathered = None
+    if args.gather and world > 1:
+        gathered = torch.empty((world, M, N), dtype=torch.float16, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    kw = dict(epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None, residual=res, out=C)
+
+    def step():
+        pax_b200.gemm(A, B, **kw)
+        if gathered is not None:
+            dist.all_gather_into_tensor(gathered, C)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record()
+        step()
+        stops[i].record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
+    ms_mean = statistics.mean(ms)
+    t = torch.tensor([ms_mean], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    flops_rank = 2.0 * M * N * K
+    value = flops_rank * world / (ms_max * 1e-3) / 1e12
+
+    # ---- end to end through the public API: pinned host inputs, host output
+    hA = A.cpu().pin_memory()
+    hB = B.cpu().pin_memory()
+    hbias = bias.cpu().pin_memory()
+    hres = res.cpu().pin_memory() if res is not None else None
+    hC = torch.empty((M, N), dtype=torch.float16).pin_memory()
+    dA, dB, dbias = torch.empty_like(A), torch.empty_like(B), torch.empty_like(bias)
+    dres = torch.empty_like(res) if res is not None else None
+    h2d = hA.numel() * 2 + hB.numel() * 2 + (hbias.numel() * 2 if "bias" in cfg["epi"] else 0) + (
+        hres.numel() * 2 if hres is not None else 0)
+    d2h = hC.numel() * 2
+
+    def e2e_step():
+        dA.copy_(hA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        if "bias" in cfg["epi"]:
+            dbias.copy_(hbias, non_blocking=True)
+        if dres is not None:
+            dres.copy_(hres, non_blocking=True)
+        pax_b200.gemm(dA, dB, epilogue=cfg["epi"], bias=dbias if "bias" in cfg["epi"] else None, residual=dres,
+                      out=C)
+        hC.copy_(C, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = flops_rank * world / (float(t.item()) * 1e-3) / 1e12
+
+    peak, hbm, peak_kind = peaks()
+    kernel_ms = min(ms) if gathered is None else None
+    achieved = flops_rank / (statistics.mean(ms) * 1e-3) / 1e12 if gathered is None else None
+    roofline = None
+    if achieved is not None:
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": traffic_from_profiles(args.config),
+                    "peak_kind": f"{peak_kind} (bf16 dense burst, MEASURED_PEAKS.json)" if peak_kind == "measured"
+                    else "fallback 1.59 PFLOP/s", "algorithmic_flops_per_launch": flops_rank,
+                    "best_launch_ms": kernel_ms}
+        if args.config == 4:
+            alg_bytes = 2 * (M * K + K * N + N + M * N)
+            gbs = alg_bytes / (statistics.mean(ms) * 1e-3) / 1e9
+            roofline = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                        "traffic": traffic_from_profiles(args.config),
+                        "peak_kind": f"{peak_kind} (copy bandwidth)", "algorithmic_bytes_per_launch": alg_bytes,
+                        "tflops": achieved}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, dt, rows, threads, kind, _ = cpu_gemm_sample(cfg, args.cpu_seconds, args.seed)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+               "sample": f"{rows} of {M} rows of the same GEMM (cpu_gemm_ref i-j-l fp32 loop) in {dt:.1f} s on "
+                         f"{threads} host threads"}
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_max,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (seeded torch RNG on device: " + (
+                "A,B uniform[-1,1]" if cfg["dist"] == "uniform" else "A N(0,1), B N(0,0.02)") + ", bias N(0,1))",
+            "config": workload_config(cfg, world, args),
+            "pct_of_dense_fp16_peak": 100.0 * (value / world) / peak,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "clocks": clk,
+            "gpu_launches": args.steps,
+            "lean_pipeline_bound": {"stages": 4, "bound_frac": 1 - 1 / 4,
+                                    "measured_frac_of_roof": (value / world) / peak},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_pax(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,276 @@
+/*
+ * pax.h -- C ABI of the pax_b200 FP16 GEMM library (NVIDIA B200, sm_100a).
+ *
+ * Drop-in for the GEMM surface of PAX's host bridge (reference project
+ * SNAPKITTYWEST/pax, file src/host_bridge.c).  Every entry point that the
+ * reference declares or defines for the GEMM path keeps its name, argument
+ * order, argument meaning and error behaviour; the citation next to each
+ * declaration names the reference interface it replaces.  Entry points marked
+ * "new" have no reference counterpart.
+ *
+ * Conventions shared by every launcher:
+ *   A  [m][k] fp16, row-major (leading dimension k unless stated)
+ *   B  [k][n] fp16, row-major (leading dimension n unless stated)
+ *   C  [m][n] row-major, fp32 in the reference-named launchers, fp16 in the
+ *      *_f16 twins
+ *   All launches are asynchronous on the caller's stream.  Launchers never
+ *   allocate caller-visible memory; the caller owns every buffer.
+ *   Launchers return void, as in the reference; a failed argument check or
+ *   launch prints "[PAX] ..." to stderr and is recorded for pax_last_error().
+ *
+ * This header is valid C99 and C++.
+ */
+#ifndef PAX_B200_PAX_H
+#define PAX_B200_PAX_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h> /* cudaStream_t; C-compatible */
+
+#ifdef __cplusplus
+#include <cuda_fp16.h>
+extern "C" {
+#else
+#ifndef PAX_HALF_DEFINED
+#define PAX_HALF_DEFINED
+/* Layout-compatible stand-in for CUDA's __half when compiling as C. */
+typedef struct { unsigned short x; } __half;
+#endif
+#endif
+
+/* ---------------------------------------------------------------------------
+ * Buffer descriptor -- identical layout to the reference
+ * (src/host_bridge.c:38-60).
+ * ------------------------------------------------------------------------- */
+typedef enum {
+    PAX_HOST    = 0,
+    PAX_DEVICE  = 1,
+    PAX_UNIFIED = 2
+} pax_ownership_t;
+
+typedef struct {
+    void*           base;
+    size_t          elem_size;
+    int64_t         shape[3];
+    int64_t         stride[3];
+    int             ndim;
+    size_t          alignment;
+    pax_ownership_t ownership;
+    cudaStream_t    stream;
+} pax_buffer_t;
+
+/* ---------------------------------------------------------------------------
+ * Status / epilogue / dtype enums (new).
+ * ------------------------------------------------------------------------- */
+typedef enum {
+    PAX_OK              = 0,
+    PAX_ERR_INVALID     = 1, /* NULL pointer, bad shape, bad stride */
+    PAX_ERR_UNSUPPORTED = 2, /* forced algorithm cannot run this problem */
+    PAX_ERR_CUDA        = 3, /* a CUDA runtime call failed */
+    PAX_ERR_TIMEOUT     = 4, /* a device-side bounded wait expired */
+    PAX_ERR_NO_DEVICE   = 5, /* no sm_100 device is current */
+    PAX_ERR_ALLOC       = 6  /* workspace allocation failed */
+} pax_status_t;
+
+typedef enum {
+    PAX_EPI_NONE               = 0, /* C = alpha*A.B                      */
+    PAX_EPI_BIAS               = 1, /* C = alpha*A.B + bias[j]            */
+    PAX_EPI_BIAS_GELU_TANH     = 2, /* C = gelu_tanh(alpha*A.B + bias[j]) */
+    PAX_EPI_BIAS_GELU_ERF      = 3, /* C = gelu_erf(alpha*A.B + bias[j])  */
+    PAX_EPI_RESIDUAL_GELU_TANH = 4, /* C = gelu_tanh(alpha*A.B + R[i][j]) */
+    PAX_EPI_RESIDUAL_GELU_ERF  = 5, /* C = gelu_erf(alpha*A.B + R[i][j])  */
+    PAX_EPI_GELU_TANH          = 6, /* C = gelu_tanh(alpha*A.B)           */
+    PAX_EPI_GELU_ERF           = 7, /* C = gelu_erf(alpha*A.B)            */
+    PAX_EPI_RESIDUAL           = 8  /* C = alpha*A.B + R[i][j]            */
+} pax_epilogue_t;
+
+typedef enum {
+    PAX_DT_F32 = 0,
+    PAX_DT_F16 = 1
+} pax_dtype_t;
+
+typedef enum {
+    PAX_ALGO_AUTO   = 0, /* pick by shape and alignment                      */
+    PAX_ALGO_TC     = 1, /* persistent tcgen05 kernel, one CTA per tile      */
+    PAX_ALGO_TC2    = 2, /* persistent tcgen05 kernel, CTA pair per tile     */
+    PAX_ALGO_SKINNY = 3, /* swap-AB stream-K tcgen05 kernel for small m      */
+    PAX_ALGO_SIMT   = 4  /* CUDA-core kernel for TMA-unaligned problems      */
+} pax_algo_t;
+
+/* General GEMM descriptor (new).  Zero leading dimensions mean contiguous. */
+typedef struct {
+    const void*    A;        /* fp16 [M][lda]                              */
+    const void*    B;        /* fp16 [K][ldb]                              */
+    void*          C;        /* c_dtype [M][ldc]                           */
+    int64_t        M, N, K;
+    int64_t        lda, ldb, ldc;
+    pax_dtype_t    c_dtype;
+    pax_epilogue_t epilogue;
+    float          alpha;    /* applied to A.B before bias/residual       */
+    const void*    bias;     /* fp16 [N]      (BIAS* epilogues)           */
+    const void*    residual; /* residual_dtype [M][ld_res] (RESIDUAL*)     */
+    pax_dtype_t    residual_dtype;
+    int64_t        ld_res;
+    pax_algo_t     algo;
+} pax_gemm_desc_t;
+
+/* ---------------------------------------------------------------------------
+ * Kernel launchers (reference-named, fp32 C).
+ * ------------------------------------------------------------------------- */
+
+/* replaces pax_gemm_wmma_launch, src/rtx_gemm_wmma.cu:107-112 (declared src/host_bridge.c:76-77) */
+void pax_gemm_wmma_launch(const __half* A, const __half* B, float* C,
+                          int m, int n, int k, cudaStream_t stream);
+
+/* replaces pax_gemm_ptx_launch, src/rtx_gemm_ptx.cu:317-331 (declared src/host_bridge.c:80-81) */
+void pax_gemm_ptx_launch(const __half* A, const __half* B, float* C,
+                         int m, int n, int k, cudaStream_t stream);
+
+/* replaces pax_gemm_ptx_smem_bytes, src/rtx_gemm_ptx.cu:308-312; returns the
+ * dynamic shared memory of the kernel that pax_gemm_ptx_launch runs. */
+size_t pax_gemm_ptx_smem_bytes(void);
+
+/* replaces pax_gemm_pipeline_launch, src/rtx_gemm_pipeline.cu:340-362 (declared src/host_bridge.c:85-87) */
+void pax_gemm_pipeline_launch(const __half* A, const __half* B, float* C,
+                              int m, int n, int k, cudaStream_t stream);
+
+/* replaces pax_gemm_pipeline_smem_bytes, src/rtx_gemm_pipeline.cu:331-334 */
+size_t pax_gemm_pipeline_smem_bytes(void);
+
+/* replaces pax_gemm_bias_gelu_launch, src/rtx_gemm_epilogue.cu:375-392 (declared src/host_bridge.c:91-94).
+ * C = gelu_tanh(A.B + bias[j]), bias fp16 [n]. */
+void pax_gemm_bias_gelu_launch(const __half* A, const __half* B, float* C,
+                               int m, int n, int k, const __half* bias,
+                               cudaStream_t stream);
+
+/* replaces pax_gemm_residual_gelu_launch, src/rtx_gemm_epilogue.cu:397-414 (declared src/host_bridge.c:95-98).
+ * C = gelu_tanh(A.B + residual[i][j]), residual fp32 [m][n]. */
+void pax_gemm_residual_gelu_launch(const __half* A, const __half* B, float* C,
+                                   int m, int n, int k, const float* residual,
+                                   cudaStream_t stream);
+
+/* replaces pax_gemm_scale_bias_gelu_launch, src/rtx_gemm_epilogue.cu:418-436 (declared src/host_bridge.c:99-102).
+ * C = gelu_tanh(alpha*A.B + bias[j]). */
+void pax_gemm_scale_bias_gelu_launch(const __half* A, const __half* B, float* C,
+                                     int m, int n, int k, float alpha,
+                                     const __half* bias, cudaStream_t stream);
+
+/* replaces pax_gemm_tma_cluster_launch, src/rtx_gemm_tma.cu:243-271.
+ * C = A.B on the CTA-pair kernel.  The tensor-map arguments are accepted for
+ * signature compatibility and ignored: tensor maps are built internally. */
+void pax_gemm_tma_cluster_launch(const __half* A, const __half* B, float* C,
+                                 int M, int N, int K,
+                                 const void* tmap_A, const void* tmap_B,
+                                 const void* tmap_C, cudaStream_t stream);
+
+/* replaces pax_gemm_tma_smem_bytes, src/rtx_gemm_tma.cu:273-275 */
+size_t pax_gemm_tma_smem_bytes(void);
+
+/* ---------------------------------------------------------------------------
+ * FP16-output twins (new; the reference writes fp32 C only).
+ * ------------------------------------------------------------------------- */
+void pax_gemm_f16_launch(const __half* A, const __half* B, __half* C,
+                         int m, int n, int k, cudaStream_t stream);
+void pax_gemm_bias_f16_launch(const __half* A, const __half* B, __half* C,
+                              int m, int n, int k, const __half* bias,
+                              cudaStream_t stream);
+void pax_gemm_bias_gelu_f16_launch(const __half* A, const __half* B, __half* C,
+                                   int m, int n, int k, const __half* bias,
+                                   cudaStream_t stream);
+void pax_gemm_bias_gelu_erf_f16_launch(const __half* A, const __half* B, __half* C,
+                                       int m, int n, int k, const __half* bias,
+                                       cudaStream_t stream);
+void pax_gemm_residual_gelu_f16_launch(const __half* A, const __half* B, __half* C,
+                                       int m, int n, int k, const __half* residual,
+                                       cudaStream_t stream);
+void pax_gemm_residual_gelu_erf_f16_launch(const __half* A, const __half* B, __half* C,
+                                           int m, int n, int k, const __half* residual,
+                                           cudaStream_t stream);
+
+/* General entry point with status return (new). */
+pax_status_t pax_gemm_ex(const pax_gemm_desc_t* desc, cudaStream_t stream);
+
+/* The algorithm pax_gemm_ex would run for desc with algo = PAX_ALGO_AUTO (new;
+ * host-only, launches nothing). */
+pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc);
+
+/* ---------------------------------------------------------------------------
+ * Host bridge (src/host_bridge.c).
+ * ------------------------------------------------------------------------- */
+
+/* replaces pax_validate_buffer, src/host_bridge.c:136-172.  1 = valid, 0 = not. */
+int pax_validate_buffer(const pax_buffer_t* buf);
+
+/* replace pax_alloc_device_1d/2d and pax_alloc_host_1d/2d, src/host_bridge.c:179-257.
+ * On failure base == NULL. */
+pax_buffer_t pax_alloc_device_1d(size_t nelems, size_t elem_size, cudaStream_t stream);
+pax_buffer_t pax_alloc_device_2d(size_t rows, size_t cols, size_t elem_size, cudaStream_t stream);
+pax_buffer_t pax_alloc_host_1d(size_t nelems, size_t elem_size, cudaStream_t stream);
+pax_buffer_t pax_alloc_host_2d(size_t rows, size_t cols, size_t elem_size, cudaStream_t stream);
+
+/* replace pax_free_device / pax_free_host, src/host_bridge.c:260-273 */
+void pax_free_device(pax_buffer_t* buf);
+void pax_free_host(pax_buffer_t* buf);
+
+/* replace pax_dispatch_{wmma,ptx,pipeline}_gemm, src/host_bridge.c:312-348.
+ * C->elem_size selects the output type: 4 = fp32 (reference), 2 = fp16.
+ * Row strides (stride[0] of 2-D buffers) are honoured. */
+void pax_dispatch_wmma_gemm(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, cudaStream_t stream);
+void pax_dispatch_ptx_gemm(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, cudaStream_t stream);
+void pax_dispatch_pipeline_gemm(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, cudaStream_t stream);
+
+/* replaces pax_dispatch_bias_gelu, src/host_bridge.c:351-366 */
+void pax_dispatch_bias_gelu(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C,
+                            const __half* bias, cudaStream_t stream);
+
+/* replaces pax_dispatch_residual_gelu, src/host_bridge.c:369-386.  residual is
+ * fp32 [m][n] as in the reference. */
+void pax_dispatch_residual_gelu(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C,
+                                const float* residual, cudaStream_t stream);
+
+/* new: the dispatcher the reference declares a launcher for but never wires
+ * (src/host_bridge.c:99-102). */
+void pax_dispatch_scale_bias_gelu(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C,
+                                  float alpha, const __half* bias, cudaStream_t stream);
+
+/* replaces cpu_gemm_ref, src/host_bridge.c:397-407: naive fp32 GEMM on the
+ * host, i-j-l loop, sequential accumulation.  Verification utility only; no
+ * GPU entry point ever calls it. */
+void cpu_gemm_ref(const float* A, const float* B, float* C, int m, int n, int k);
+
+/* replaces pax_verify_gemm, src/host_bridge.c:422-445: max relative error
+ * |g-r|/(|r|+1e-8) <= tol prints PASS and returns 1, else FAIL and 0. */
+int pax_verify_gemm(const float* C_gpu, const float* C_ref, int m, int n, float tol);
+
+/* replaces pax_bench_all, src/host_bridge.c:543-566: times every variant on
+ * the state set by pax_bench_setup and prints ms/iter and TFLOP/s. */
+void pax_bench_all(int iters);
+
+/* new: the reference keeps its bench state in file-static globals
+ * (src/host_bridge.c:487-500) with no setter; these allocate and release it. */
+int  pax_bench_setup(int m, int n, int k, cudaStream_t stream);
+void pax_bench_teardown(void);
+
+/* ---------------------------------------------------------------------------
+ * Status and lifetime (new).
+ * ------------------------------------------------------------------------- */
+pax_status_t pax_last_error(void);               /* thread-local, last call */
+const char*  pax_status_string(pax_status_t s);
+/* Reads and clears the device-side error word of the current device
+ * (synchronises the device).  Returns PAX_ERR_TIMEOUT if a bounded wait in a
+ * kernel expired since the last read, else PAX_OK. */
+pax_status_t pax_device_error(void);
+/* Frees the per-stream split-K workspaces this library allocated. */
+void         pax_shutdown(void);
+/* Library version string. */
+const char*  pax_version(void);
+/* sizeof(pax_buffer_t) and sizeof(pax_gemm_desc_t) as compiled into the
+ * library, so that bindings can check their struct layouts. */
+size_t       pax_sizeof_buffer(void);
+size_t       pax_sizeof_gemm_desc(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* PAX_B200_PAX_H */

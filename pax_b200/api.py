@@ -1,0 +1,132 @@
+"""Tensor-level front end of the C ABI: ``gemm(A, B, ...)`` on torch CUDA
+tensors.  torch supplies device memory and the stream; every FLOP runs in
+libpax_b200.so (pax_gemm_ex)."""
+from __future__ import annotations
+
+import ctypes
+from enum import IntEnum
+
+import torch
+
+from ._lib import GemmDesc, lib
+
+
+class Status(IntEnum):
+    OK = 0
+    INVALID = 1
+    UNSUPPORTED = 2
+    CUDA = 3
+    TIMEOUT = 4
+    NO_DEVICE = 5
+    ALLOC = 6
+
+
+class Epilogue(IntEnum):
+    NONE = 0
+    BIAS = 1
+    BIAS_GELU_TANH = 2
+    BIAS_GELU_ERF = 3
+    RESIDUAL_GELU_TANH = 4
+    RESIDUAL_GELU_ERF = 5
+    GELU_TANH = 6
+    GELU_ERF = 7
+    RESIDUAL = 8
+
+
+class DType(IntEnum):
+    F32 = 0
+    F16 = 1
+
+
+class Algo(IntEnum):
+    AUTO = 0
+    TC = 1
+    TC2 = 2
+    SKINNY = 3
+    SIMT = 4
+
+
+class PaxError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = Status(status)
+        msg = lib.pax_status_string(int(status)).decode()
+        super().__init__(f"{what}: {msg} ({self.status.name})" if what else msg)
+
+
+_EPI_NAMES = {e.name.lower(): e for e in Epilogue}
+_DT = {torch.float32: DType.F32, torch.float16: DType.F16}
+
+
+def _row_major_ld(t: torch.Tensor, name: str) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D tensor with unit column stride")
+    return t.stride(0)
+
+
+def make_desc(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, epilogue="none", bias=None, residual=None,
+              alpha: float = 1.0, algo="auto") -> GemmDesc:
+    epi = _EPI_NAMES[epilogue] if isinstance(epilogue, str) else Epilogue(epilogue)
+    al = Algo[algo.upper()] if isinstance(algo, str) else Algo(algo)
+    if A.dtype != torch.float16 or B.dtype != torch.float16:
+        raise TypeError("A and B must be float16")
+    if C.dtype not in _DT:
+        raise TypeError("C must be float32 or float16")
+    M, K = A.shape
+    K2, N = B.shape
+    if K2 != K or tuple(C.shape) != (M, N):
+        raise ValueError(f"shape mismatch: A {tuple(A.shape)} B {tuple(B.shape)} C {tuple(C.shape)}")
+    d = GemmDesc()
+    d.A, d.B, d.C = A.data_ptr(), B.data_ptr(), C.data_ptr()
+    d.M, d.N, d.K = M, N, K
+    d.lda = _row_major_ld(A, "A") if A.numel() else 0
+    d.ldb = _row_major_ld(B, "B") if B.numel() else 0
+    d.ldc = _row_major_ld(C, "C") if C.numel() else 0
+    d.c_dtype = int(_DT[C.dtype])
+    d.epilogue = int(epi)
+    d.alpha = float(alpha)
+    if bias is not None:
+        if bias.dtype != torch.float16 or bias.numel() != N:
+            raise ValueError("bias must be float16 with N elements")
+        d.bias = bias.data_ptr()
+    if residual is not None:
+        if residual.dtype not in _DT or tuple(residual.shape) != (M, N):
+            raise ValueError("residual must be float32/float16 of shape (M, N)")
+        d.residual = residual.data_ptr()
+        d.residual_dtype = int(_DT[residual.dtype])
+        d.ld_res = _row_major_ld(residual, "residual")
+    d.algo = int(al)
+    return d
+
+
+def gemm(A: torch.Tensor, B: torch.Tensor, *, epilogue="none", bias=None, residual=None, alpha: float = 1.0,
+         out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16, algo="auto",
+         stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """C = epilogue(alpha * A @ B) on the current (or given) CUDA stream.
+
+    A [M, K] and B [K, N] are float16 row-major CUDA tensors; C is float16 or
+    float32.  epilogue is one of none, bias, bias_gelu_tanh, bias_gelu_erf,
+    residual_gelu_tanh, residual_gelu_erf, gelu_tanh, gelu_erf, residual.
+    """
+    if out is None:
+        out = torch.empty((A.shape[0], B.shape[1]), dtype=out_dtype, device=A.device)
+    d = make_desc(A, B, out, epilogue, bias, residual, alpha, algo)
+    s = stream if stream is not None else torch.cuda.current_stream(A.device)
+    st = lib.pax_gemm_ex(ctypes.byref(d), ctypes.c_void_p(s.cuda_stream))
+    if st != 0:
+        raise PaxError(st, "pax_gemm_ex")
+    return out
+
+
+def select_algo(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, **kw) -> Algo:
+    """The algorithm pax_gemm_ex would run (host-only)."""
+    d = make_desc(A, B, C, **kw)
+    return Algo(lib.pax_gemm_select_algo(ctypes.byref(d)))
+
+
+def device_error() -> Status:
+    """Read and clear the device error word (synchronises the device)."""
+    return Status(lib.pax_device_error())
+
+
+def last_error() -> Status:
+    return Status(lib.pax_last_error())

@@ -1,0 +1,394 @@
+// gemm_skinny.cu -- swap-AB stream-K tcgen05 GEMM for small M (decode shapes).
+//
+//   C[M][N] = epi(A[M][K] . B[K][N]), M <= 64.  The reference has no separate
+//   skinny path: its kernels tile M by 128 and would leave most of every tile
+//   empty (src/rtx_gemm_epilogue.cu:362-366).  Here the product is computed
+//   transposed, C^T = B^T . A^T, so N supplies the 128-row MMA dimension and
+//   M (padded to MP, a multiple of 16) the MMA N dimension:
+//     MMA A operand: B^T tile, 128 n x 64 k, read N-major straight from B.
+//     MMA B operand: A tile, MP rows x 64 k, K-major.
+//   The work (N/128 column tiles x K/64 k-blocks) is cut into equal
+//   contiguous ranges, one per persistent CTA, so every SM streams the same
+//   number of bytes of B (stream-K).  A column tile split between CTAs is
+//   finished by whichever contributor arrives last: partial sums go to a
+//   per-CTA workspace slot and the last arriver adds them in CTA order, so the
+//   result does not depend on arrival order.
+//
+// Warp roles as in gemm_tc.cu: warp 0 TMA, warp 1 MMA + TMEM, warps 2..5
+// epilogue.
+#include "internal.h"
+#include "sm100.cuh"
+#include "epilogue.cuh"
+
+#include <cudaTypedefs.h>
+#include <mutex>
+
+namespace pax {
+
+struct SkinnyParams {
+    int M, N, K;
+    int num_tiles;  // ceil(N / 128)
+    int kblocks;    // ceil(K / 64)
+    long long work; // num_tiles * kblocks
+    int grid;       // number of CTAs (<= work)
+    float* ws;      // [grid][2][MP][128] fp32 partial sums
+    int* counters;  // [num_tiles], zero between launches
+    __half* c16;    // exactly one of c16 / c32 is set
+    float* c32;
+    long long ldc;
+    EpiParams epi;
+};
+
+template <int MP_>
+struct SkCfg {
+    static constexpr int MP = MP_, BK = 64, TN = 128;
+    static constexpr uint32_t B_BYTES = TN * BK * 2;   // 16 KiB: two 64n x 64k boxes
+    static constexpr uint32_t A_BYTES = MP * BK * 2;   // MP rows of 128 bytes
+    static constexpr uint32_t STAGE_BYTES = B_BYTES + A_BYTES;
+    static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
+    static constexpr uint32_t TMEM_COLS = (2 * MP <= 32) ? 32 : (2 * MP <= 64) ? 64 : 128;
+    static constexpr uint32_t ACC_STRIDE = TMEM_COLS / 2;  // column offset of accumulator 1
+    static constexpr uint32_t NUM_BARS = 2 * STAGES + 5;
+    static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + NUM_BARS * 8 + 16;
+    static constexpr uint32_t IDESC = umma_idesc_f16(128, MP, /*a_mn*/ true, /*b_mn*/ false);
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+    static_assert(A_BYTES % 1024 == 0, "A slot must keep 1024-byte swizzle alignment");
+};
+
+__device__ __forceinline__ long long sk_unit_begin(long long c, const SkinnyParams& p) {
+    return c * p.work / p.grid;
+}
+// CTA whose unit range contains unit x.
+__device__ __forceinline__ int sk_owner(long long x, const SkinnyParams& p) {
+    return (int)(((x + 1) * p.grid + p.work - 1) / p.work - 1);
+}
+
+template <int MP>
+__global__ void __launch_bounds__(192, 1)
+    gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const SkinnyParams p) {
+    using Cfg = SkCfg<MP>;
+    constexpr int STAGES = Cfg::STAGES;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem =
+        reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sB = smem;                              // [STAGES][B_BYTES]
+    uint8_t* sA = sB + STAGES * Cfg::B_BYTES;        // [STAGES][A_BYTES]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sA + STAGES * Cfg::A_BYTES);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NUM_BARS);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+    const uint32_t bar0 = smem_u32(bars);
+    const uint32_t full0 = bar0;
+    const uint32_t empty0 = bar0 + 8u * STAGES;
+    const uint32_t tfull0 = bar0 + 16u * STAGES;
+    const uint32_t tempty0 = tfull0 + 16u;
+    const uint32_t drain_bar = tempty0 + 16u;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const long long ub = sk_unit_begin(blockIdx.x, p);
+    const long long ue = sk_unit_begin(blockIdx.x + 1, p);
+    const int KB = p.kblocks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full0 + 8u * s, 1);
+            mbar_init(empty0 + 8u * s, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull0 + 8u * b, 1);
+            mbar_init(tempty0 + 8u * b, 4);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc<1>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+        tmem_relinquish<1>();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0, last_parity = 0;
+            bool ok = true;
+            for (long long u = ub; u < ue; ++u) {
+                const int tile = (int)(u / KB);
+                const int kb = (int)(u - (long long)tile * KB);
+                if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t fb = full0 + 8u * stage;
+                mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+                const uint32_t bdst = smem_u32(sB + stage * Cfg::B_BYTES);
+                tma_load_2d(bdst, &tmB, fb, tile * 128, kb * 64);
+                tma_load_2d(bdst + 8192u, &tmB, fb, tile * 128 + 64, kb * 64);
+                tma_load_2d(smem_u32(sA + stage * Cfg::A_BYTES), &tmA, fb, kb * 64, 0);
+                issued |= 1u << stage;
+                last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok)
+                for (int s = 0; s < STAGES; ++s)
+                    if (issued & (1u << s)) mbar_wait(full0 + 8u * s, (last_parity >> s) & 1u, nullptr);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            long long u = ub;
+            while (ok && u < ue) {
+                const int tile = (int)(u / KB);
+                const long long seg_end = min(ue, (long long)(tile + 1) * KB);
+                if (!mbar_wait(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)acc * Cfg::ACC_STRIDE;
+                for (long long v = u; v < seg_end; ++v) {
+                    if (!mbar_wait(full0 + 8u * stage, phase, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t b0 = smem_u32(sB + stage * Cfg::B_BYTES);
+                    const uint32_t a0 = smem_u32(sA + stage * Cfg::A_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t ad = umma_desc_sw128(b0 + kk * 2048, 8192, 1024);  // B^T, N-major
+                        const uint64_t bd = umma_desc_sw128(a0 + kk * 32, 16, 1024);      // A, K-major
+                        tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (v != u || kk != 0) ? 1u : 0u);
+                    }
+                    tc_commit(empty0 + 8u * stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(tfull0 + 8u * acc);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+                u = seg_end;
+            }
+            tc_commit(drain_bar);
+            mbar_wait(drain_bar, 0, nullptr);
+        }
+    } else {
+        const int q = warp & 3;
+        const int et = threadIdx.x - 64;  // 0..127 among epilogue threads
+        const int n_local = q * 32 + lane;
+        const int first_tile = (int)(ub / KB);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        long long u = ub;
+        while (u < ue) {
+            const int tile = (int)(u / KB);
+            const long long seg_begin = u;
+            const long long seg_end = min(ue, (long long)(tile + 1) * KB);
+            u = seg_end;
+            // All four epilogue warps take the same branch (they meet at named
+            // barriers below), so the wait outcome is AND-reduced across them.
+            const uint32_t ok_local = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag) ? 1u : 0u;
+            uint32_t ok_all;
+            asm volatile(
+                "{\n\t.reg .pred p, q;\n\t"
+                "setp.ne.u32 p, %1, 0;\n\t"
+                "bar.red.and.pred q, 1, 128, p;\n\t"
+                "selp.u32 %0, 1, 0, q;\n\t}"
+                : "=r"(ok_all)
+                : "r"(ok_local)
+                : "memory");
+            if (!ok_all) break;
+            tc_fence_after();
+            float v[MP];
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)acc * Cfg::ACC_STRIDE;
+#pragma unroll
+            for (int j = 0; j < MP / 16; ++j) tmem_ld_32x32b_x16(t_row + 16u * j, v + 16 * j);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty0 + 8u * acc);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+
+            const long long n = (long long)tile * 128 + n_local;
+            const bool whole = (seg_begin == (long long)tile * KB) && (seg_end == (long long)(tile + 1) * KB);
+            bool do_out = whole;
+            if (!whole) {
+                // Park the partial sum, then count contributions for this tile.
+                const int slot = (tile == first_tile) ? 0 : 1;
+                float* wp = p.ws + ((size_t)blockIdx.x * 2 + slot) * (size_t)(MP * 128);
+#pragma unroll
+                for (int m = 0; m < MP; ++m) wp[m * 128 + n_local] = v[m];
+                __threadfence();
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (et == 0) {
+                    const int c_first = sk_owner((long long)tile * KB, p);
+                    const int c_last = sk_owner((long long)(tile + 1) * KB - 1, p);
+                    const int prev = atomicAdd(p.counters + tile, 1);
+                    const int is_last = (prev == c_last - c_first) ? 1 : 0;
+                    if (is_last) p.counters[tile] = 0;  // ready for the next launch
+                    *last_flag = is_last;
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                do_out = (*last_flag != 0);
+                // Every epilogue thread has read the flag before it is reused.
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (do_out) {
+                    __threadfence();
+                    const int c_first = sk_owner((long long)tile * KB, p);
+                    const int c_last = sk_owner((long long)(tile + 1) * KB - 1, p);
+#pragma unroll
+                    for (int m = 0; m < MP; ++m) v[m] = 0.f;
+                    for (int c = c_first; c <= c_last; ++c) {
+                        const int cs = ((int)(sk_unit_begin(c, p) / KB) == tile) ? 0 : 1;
+                        const float* rp = p.ws + ((size_t)c * 2 + cs) * (size_t)(MP * 128);
+#pragma unroll
+                        for (int m = 0; m < MP; ++m) v[m] += __ldcg(rp + m * 128 + n_local);
+                    }
+                }
+            }
+            if (do_out && n < p.N) {
+                const int flags = p.epi.flags;
+                const float b = (flags & EPI_BIAS) ? __half2float(p.epi.bias[n]) : 0.f;
+#pragma unroll
+                for (int m = 0; m < MP; ++m) {
+                    if (m < p.M) {
+                        float r = 0.f;
+                        if (flags & EPI_RES) {
+                            const long long off = (long long)m * p.epi.ld_res + n;
+                            r = (flags & EPI_RES_F32) ? static_cast<const float*>(p.epi.residual)[off]
+                                                      : __half2float(static_cast<const __half*>(p.epi.residual)[off]);
+                        }
+                        const float o = epi_scalar(v[m], b, r, flags, p.epi.alpha);
+                        if (p.c16)
+                            p.c16[(long long)m * p.ldc + n] = __float2half_rn(o);
+                        else
+                            p.c32[(long long)m * p.ldc + n] = o;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc<1>(tmem_base, Cfg::TMEM_COLS);
+    }
+}
+
+// ======================================================================
+// Host side
+// ======================================================================
+
+static PFN_cuTensorMapEncodeTiled_v12000 sk_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+static bool sk_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch_bytes,
+                    uint32_t box_inner, uint32_t box_outer) {
+    auto enc = sk_encoder();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {pitch_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int skinny_mp(long long M) { return (int)((M + 15) / 16) * 16; }
+
+void skinny_geometry(long long M, long long N, long long K, int sms, int* grid, size_t* ws_bytes,
+                     size_t* counter_bytes) {
+    const long long tiles = (N + 127) / 128;
+    const long long work = tiles * ((K + 63) / 64);
+    long long g = sms;
+    if (g > work) g = work;
+    if (g < 1) g = 1;
+    *grid = (int)g;
+    *ws_bytes = (size_t)g * 2 * (size_t)skinny_mp(M) * 128 * sizeof(float);
+    *counter_bytes = (size_t)tiles * sizeof(int);
+}
+
+template <int MP>
+static pax_status_t launch_skinny_impl(const Problem& pr, int grid, float* ws, int* counters,
+                                       cudaStream_t stream) {
+    using Cfg = SkCfg<MP>;
+    CUtensorMap tA, tB;
+    if (!sk_tmap(&tA, pr.A, pr.K, pr.M, pr.lda * 2, 64, MP)) return PAX_ERR_CUDA;
+    if (!sk_tmap(&tB, pr.B, pr.N, pr.K, pr.ldb * 2, 64, 64)) return PAX_ERR_CUDA;
+    SkinnyParams p;
+    p.M = (int)pr.M;
+    p.N = (int)pr.N;
+    p.K = (int)pr.K;
+    p.num_tiles = (int)((pr.N + 127) / 128);
+    p.kblocks = (int)((pr.K + 63) / 64);
+    p.work = (long long)p.num_tiles * p.kblocks;
+    p.grid = grid;
+    p.ws = ws;
+    p.counters = counters;
+    p.c16 = pr.c_f16 ? static_cast<__half*>(pr.C) : nullptr;
+    p.c32 = pr.c_f16 ? nullptr : static_cast<float*>(pr.C);
+    p.ldc = pr.ldc;
+    p.epi = pr.epi;
+    auto kern = gemm_skinny_kernel<MP>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES) != cudaSuccess)
+        return PAX_ERR_CUDA;
+    kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(tA, tB, p);
+    return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
+}
+
+pax_status_t launch_skinny_ws(const Problem& p, int grid, float* ws, int* counters, cudaStream_t stream) {
+    if (p.M < 1 || p.M > kSkinnyMaxM || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
+    switch (skinny_mp(p.M)) {
+        case 16: return launch_skinny_impl<16>(p, grid, ws, counters, stream);
+        case 32: return launch_skinny_impl<32>(p, grid, ws, counters, stream);
+        case 48: return launch_skinny_impl<48>(p, grid, ws, counters, stream);
+        default: return launch_skinny_impl<64>(p, grid, ws, counters, stream);
+    }
+}
+
+int read_clear_device_error_skinny() {
+    int v = 0, z = 0;
+    if (cudaMemcpyFromSymbol(&v, g_pax_device_error, sizeof(int)) != cudaSuccess) return -1;
+    if (v) cudaMemcpyToSymbol(g_pax_device_error, &z, sizeof(int));
+    return v;
+}
+
+}  // namespace pax

@@ -1,0 +1,759 @@
+// host_bridge.cpp -- the C ABI (include/pax.h) over the sm_100a kernels.
+//
+// Mirrors the GEMM surface of the reference's host bridge (src/host_bridge.c):
+// buffer descriptor helpers (:136-273), per-variant dispatchers (:311-386),
+// the CPU verification GEMM and checker (:397-445) and the bench harness
+// (:452-566), plus the kernel launchers the bridge declares (:75-102).
+// Argument checks print "[PAX] ..." to stderr and return, as the reference
+// does; every entry point also records a status for pax_last_error().
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "../../include/pax.h"
+#include "internal.h"
+
+namespace pax {
+
+static thread_local pax_status_t t_last = PAX_OK;
+
+static pax_status_t set_status(pax_status_t s) {
+    t_last = s;
+    return s;
+}
+
+static pax_status_t fail(pax_status_t s, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    fprintf(stderr, "[PAX] ");
+    vfprintf(stderr, fmt, ap);
+    fprintf(stderr, "\n");
+    va_end(ap);
+    return set_status(s);
+}
+
+// ------------------------------------------------------------ devices
+struct DevInfo {
+    int sms = 0;
+    int major = 0;
+    int minor = 0;
+    bool known = false;
+};
+static std::mutex g_dev_mu;
+static std::map<int, DevInfo> g_dev;
+
+static DevInfo device_info(int dev) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DevInfo& d = g_dev[dev];
+    if (!d.known) {
+        cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+        d.known = true;
+    }
+    return d;
+}
+
+int current_device() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return dev;
+}
+
+int device_sm_count(int dev) { return device_info(dev).sms; }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool tma_compatible(const Problem& p) {
+    const long long csz = p.c_f16 ? 2 : 4;
+    return p.K >= 1 && aligned16(p.A) && aligned16(p.B) && aligned16(p.C) && (p.lda * 2) % 16 == 0 &&
+           (p.ldb * 2) % 16 == 0 && (p.ldc * csz) % 16 == 0 && p.M < (1LL << 31) && p.N < (1LL << 31) &&
+           p.K < (1LL << 31);
+}
+
+// --------------------------------------------------------- workspaces
+// Split-K partial sums of the skinny kernel, one buffer per (device, stream)
+// so that launches on different streams never share one.  Layout:
+// [counters, padded to 256 B][partial sums].
+struct Workspace {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+static std::mutex g_ws_mu;
+static std::map<std::pair<int, uintptr_t>, Workspace> g_ws;
+
+static pax_status_t get_workspace(int dev, cudaStream_t s, size_t need, void** out) {
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    Workspace& w = g_ws[{dev, reinterpret_cast<uintptr_t>(s)}];
+    if (w.bytes < need) {
+        if (w.ptr) {
+            cudaStreamSynchronize(s);
+            cudaFree(w.ptr);
+            w.ptr = nullptr;
+            w.bytes = 0;
+        }
+        if (cudaMalloc(&w.ptr, need) != cudaSuccess) {
+            w.ptr = nullptr;
+            return PAX_ERR_ALLOC;
+        }
+        if (cudaMemsetAsync(w.ptr, 0, need, s) != cudaSuccess) return PAX_ERR_CUDA;
+        w.bytes = need;
+    }
+    *out = w.ptr;
+    return PAX_OK;
+}
+
+static void free_workspaces() {
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    int prev = current_device();
+    for (auto& kv : g_ws) {
+        if (kv.second.ptr) {
+            cudaSetDevice(kv.first.first);
+            cudaDeviceSynchronize();
+            cudaFree(kv.second.ptr);
+        }
+    }
+    g_ws.clear();
+    cudaSetDevice(prev);
+}
+
+// ------------------------------------------------------------ problems
+static int epilogue_flags(pax_epilogue_t e, pax_dtype_t res_dt, float alpha) {
+    int f = 0;
+    switch (e) {
+        case PAX_EPI_NONE: break;
+        case PAX_EPI_BIAS: f = EPI_BIAS; break;
+        case PAX_EPI_BIAS_GELU_TANH: f = EPI_BIAS | EPI_GELU_TANH; break;
+        case PAX_EPI_BIAS_GELU_ERF: f = EPI_BIAS | EPI_GELU_ERF; break;
+        case PAX_EPI_RESIDUAL_GELU_TANH: f = EPI_RES | EPI_GELU_TANH; break;
+        case PAX_EPI_RESIDUAL_GELU_ERF: f = EPI_RES | EPI_GELU_ERF; break;
+        case PAX_EPI_GELU_TANH: f = EPI_GELU_TANH; break;
+        case PAX_EPI_GELU_ERF: f = EPI_GELU_ERF; break;
+        case PAX_EPI_RESIDUAL: f = EPI_RES; break;
+        default: return -1;
+    }
+    if ((f & EPI_RES) && res_dt == PAX_DT_F32) f |= EPI_RES_F32;
+    if (alpha != 1.0f) f |= EPI_SCALE;
+    return f;
+}
+
+static pax_status_t normalize(const pax_gemm_desc_t* d, Problem* p) {
+    if (!d) return fail(PAX_ERR_INVALID, "pax_gemm_ex: NULL descriptor");
+    if (d->M < 0 || d->N < 0 || d->K < 0)
+        return fail(PAX_ERR_INVALID, "pax_gemm_ex: negative shape m=%lld n=%lld k=%lld", (long long)d->M,
+                    (long long)d->N, (long long)d->K);
+    if (d->c_dtype != PAX_DT_F32 && d->c_dtype != PAX_DT_F16)
+        return fail(PAX_ERR_INVALID, "pax_gemm_ex: bad output dtype %d", (int)d->c_dtype);
+    const int flags = epilogue_flags(d->epilogue, d->residual_dtype, d->alpha);
+    if (flags < 0) return fail(PAX_ERR_INVALID, "pax_gemm_ex: bad epilogue %d", (int)d->epilogue);
+    p->A = static_cast<const __half*>(d->A);
+    p->B = static_cast<const __half*>(d->B);
+    p->C = d->C;
+    p->M = d->M;
+    p->N = d->N;
+    p->K = d->K;
+    p->lda = d->lda ? d->lda : d->K;
+    p->ldb = d->ldb ? d->ldb : d->N;
+    p->ldc = d->ldc ? d->ldc : d->N;
+    p->c_f16 = d->c_dtype == PAX_DT_F16;
+    p->epi.bias = static_cast<const __half*>(d->bias);
+    p->epi.residual = d->residual;
+    p->epi.ld_res = d->ld_res ? d->ld_res : d->N;
+    p->epi.alpha = d->alpha;
+    p->epi.flags = flags;
+    if (p->M == 0 || p->N == 0) return PAX_OK;  // nothing to write
+    if (!p->C) return fail(PAX_ERR_INVALID, "pax_gemm_ex: NULL C");
+    if (p->K > 0 && (!p->A || !p->B)) return fail(PAX_ERR_INVALID, "pax_gemm_ex: NULL A or B");
+    if ((flags & EPI_BIAS) && !p->epi.bias) return fail(PAX_ERR_INVALID, "pax_gemm_ex: NULL bias");
+    if ((flags & EPI_RES) && !p->epi.residual) return fail(PAX_ERR_INVALID, "pax_gemm_ex: NULL residual");
+    if ((flags & EPI_RES) && d->residual_dtype != PAX_DT_F32 && d->residual_dtype != PAX_DT_F16)
+        return fail(PAX_ERR_INVALID, "pax_gemm_ex: bad residual dtype %d", (int)d->residual_dtype);
+    if (p->lda < p->K || p->ldb < p->N || p->ldc < p->N || ((flags & EPI_RES) && p->epi.ld_res < p->N))
+        return fail(PAX_ERR_INVALID, "pax_gemm_ex: leading dimension smaller than the row length");
+    if (aligned16(p->epi.bias)) p->epi.flags |= EPI_BIAS_VEC;
+    const long long rsz = (flags & EPI_RES_F32) ? 4 : 2;
+    if ((flags & EPI_RES) && aligned16(p->epi.residual) && (p->epi.ld_res * rsz) % 16 == 0)
+        p->epi.flags |= EPI_RES_VEC;
+    return PAX_OK;
+}
+
+static pax_algo_t select_algo(const Problem& p) {
+    if (!tma_compatible(p)) return PAX_ALGO_SIMT;
+    if (p.M <= kSkinnyMaxM) return PAX_ALGO_SKINNY;
+    return PAX_ALGO_TC;
+}
+
+static int env_int(const char* name, int dflt) {
+    const char* v = getenv(name);
+    return v ? atoi(v) : dflt;
+}
+
+static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
+    if (p.M == 0 || p.N == 0) return PAX_OK;
+    const int dev = current_device();
+    const DevInfo di = device_info(dev);
+    if (di.major != 10) return fail(PAX_ERR_NO_DEVICE, "device %d is sm_%d%d; this library needs sm_100", dev,
+                                    di.major, di.minor);
+    if (algo == PAX_ALGO_AUTO) algo = select_algo(p);
+    pax_status_t st;
+    switch (algo) {
+        case PAX_ALGO_TC:
+        case PAX_ALGO_TC2: {
+            if (!tma_compatible(p)) return fail(PAX_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned rows");
+            int bn = env_int("PAX_TC_BN", 0);
+            if (bn != 128 && bn != 256) bn = tc_pick_bn(p.M, p.N, di.sms);
+            st = launch_tc(p, bn, s);
+            break;
+        }
+        case PAX_ALGO_SKINNY: {
+            if (!tma_compatible(p) || p.M > kSkinnyMaxM)
+                return fail(PAX_ERR_UNSUPPORTED, "skinny path needs m <= %lld and 16-byte aligned rows",
+                            kSkinnyMaxM);
+            int grid;
+            size_t ws_bytes, cnt_bytes;
+            skinny_geometry(p.M, p.N, p.K, di.sms, &grid, &ws_bytes, &cnt_bytes);
+            const size_t cnt_pad = (cnt_bytes + 255) & ~size_t(255);
+            void* ws = nullptr;
+            st = get_workspace(dev, s, cnt_pad + ws_bytes, &ws);
+            if (st != PAX_OK) return fail(st, "skinny workspace allocation failed (%zu bytes)", cnt_pad + ws_bytes);
+            st = launch_skinny_ws(p, grid, reinterpret_cast<float*>(static_cast<char*>(ws) + cnt_pad),
+                                  static_cast<int*>(ws), s);
+            break;
+        }
+        case PAX_ALGO_SIMT: st = launch_simt(p, s); break;
+        default: return fail(PAX_ERR_INVALID, "unknown algorithm %d", (int)algo);
+    }
+    if (st != PAX_OK) return fail(st, "launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return set_status(PAX_OK);
+}
+
+static pax_status_t gemm_simple(const void* A, const void* B, void* C, int m, int n, int k, pax_dtype_t cdt,
+                                pax_epilogue_t epi, float alpha, const void* bias, const void* residual,
+                                pax_dtype_t rdt, cudaStream_t s, const char* who) {
+    if (m < 0 || n < 0 || k < 0) return fail(PAX_ERR_INVALID, "%s: negative shape m=%d n=%d k=%d", who, m, n, k);
+    pax_gemm_desc_t d;
+    memset(&d, 0, sizeof(d));
+    d.A = A;
+    d.B = B;
+    d.C = C;
+    d.M = m;
+    d.N = n;
+    d.K = k;
+    d.c_dtype = cdt;
+    d.epilogue = epi;
+    d.alpha = alpha;
+    d.bias = bias;
+    d.residual = residual;
+    d.residual_dtype = rdt;
+    d.algo = PAX_ALGO_AUTO;
+    return pax_gemm_ex(&d, s);
+}
+
+}  // namespace pax
+
+using namespace pax;
+
+extern "C" {
+
+// ================================================================ status
+const char* pax_version(void) { return "pax_b200 0.1.0 (sm_100a)"; }
+
+pax_status_t pax_last_error(void) { return t_last; }
+
+const char* pax_status_string(pax_status_t s) {
+    switch (s) {
+        case PAX_OK: return "ok";
+        case PAX_ERR_INVALID: return "invalid argument";
+        case PAX_ERR_UNSUPPORTED: return "unsupported problem for the requested algorithm";
+        case PAX_ERR_CUDA: return "CUDA error";
+        case PAX_ERR_TIMEOUT: return "device-side wait timed out";
+        case PAX_ERR_NO_DEVICE: return "no sm_100 device";
+        case PAX_ERR_ALLOC: return "workspace allocation failed";
+    }
+    return "unknown status";
+}
+
+pax_status_t pax_device_error(void) {
+    if (cudaDeviceSynchronize() != cudaSuccess) return set_status(PAX_ERR_CUDA);
+    const int a = read_clear_device_error_tc();
+    const int b = read_clear_device_error_skinny();
+    if (a < 0 || b < 0) return set_status(PAX_ERR_CUDA);
+    return set_status((a | b) ? PAX_ERR_TIMEOUT : PAX_OK);
+}
+
+void pax_shutdown(void) { free_workspaces(); }
+
+size_t pax_sizeof_buffer(void) { return sizeof(pax_buffer_t); }
+size_t pax_sizeof_gemm_desc(void) { return sizeof(pax_gemm_desc_t); }
+
+// ================================================================ general
+pax_status_t pax_gemm_ex(const pax_gemm_desc_t* desc, cudaStream_t stream) {
+    Problem p;
+    pax_status_t st = normalize(desc, &p);
+    if (st != PAX_OK) return st;
+    return run(p, desc->algo, stream);
+}
+
+pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc) {
+    Problem p;
+    if (normalize(desc, &p) != PAX_OK) return PAX_ALGO_AUTO;
+    set_status(PAX_OK);
+    return select_algo(p);
+}
+
+// ======================================================= reference launchers
+void pax_gemm_wmma_launch(const __half* A, const __half* B, float* C, int m, int n, int k, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F32, PAX_EPI_NONE, 1.f, nullptr, nullptr, PAX_DT_F32, s,
+                "pax_gemm_wmma_launch");
+}
+void pax_gemm_ptx_launch(const __half* A, const __half* B, float* C, int m, int n, int k, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F32, PAX_EPI_NONE, 1.f, nullptr, nullptr, PAX_DT_F32, s,
+                "pax_gemm_ptx_launch");
+}
+void pax_gemm_pipeline_launch(const __half* A, const __half* B, float* C, int m, int n, int k, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F32, PAX_EPI_NONE, 1.f, nullptr, nullptr, PAX_DT_F32, s,
+                "pax_gemm_pipeline_launch");
+}
+size_t pax_gemm_ptx_smem_bytes(void) { return tc_smem_bytes(256, false); }
+size_t pax_gemm_pipeline_smem_bytes(void) { return tc_smem_bytes(256, false); }
+size_t pax_gemm_tma_smem_bytes(void) { return tc_smem_bytes(256, false); }
+
+void pax_gemm_bias_gelu_launch(const __half* A, const __half* B, float* C, int m, int n, int k,
+                               const __half* bias, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F32, PAX_EPI_BIAS_GELU_TANH, 1.f, bias, nullptr, PAX_DT_F32, s,
+                "pax_gemm_bias_gelu_launch");
+}
+void pax_gemm_residual_gelu_launch(const __half* A, const __half* B, float* C, int m, int n, int k,
+                                   const float* residual, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F32, PAX_EPI_RESIDUAL_GELU_TANH, 1.f, nullptr, residual, PAX_DT_F32, s,
+                "pax_gemm_residual_gelu_launch");
+}
+void pax_gemm_scale_bias_gelu_launch(const __half* A, const __half* B, float* C, int m, int n, int k,
+                                     float alpha, const __half* bias, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F32, PAX_EPI_BIAS_GELU_TANH, alpha, bias, nullptr, PAX_DT_F32, s,
+                "pax_gemm_scale_bias_gelu_launch");
+}
+void pax_gemm_tma_cluster_launch(const __half* A, const __half* B, float* C, int M, int N, int K,
+                                 const void* tmap_A, const void* tmap_B, const void* tmap_C, cudaStream_t s) {
+    (void)tmap_A;
+    (void)tmap_B;
+    (void)tmap_C;
+    if (M < 0 || N < 0 || K < 0) {
+        fail(PAX_ERR_INVALID, "pax_gemm_tma_cluster_launch: negative shape");
+        return;
+    }
+    pax_gemm_desc_t d;
+    memset(&d, 0, sizeof(d));
+    d.A = A;
+    d.B = B;
+    d.C = C;
+    d.M = M;
+    d.N = N;
+    d.K = K;
+    d.c_dtype = PAX_DT_F32;
+    d.epilogue = PAX_EPI_NONE;
+    d.alpha = 1.f;
+    d.algo = PAX_ALGO_TC2;
+    Problem p;
+    if (normalize(&d, &p) != PAX_OK) return;
+    // Problems the tensor-core path cannot take still get an answer.
+    run(p, tma_compatible(p) ? PAX_ALGO_TC2 : PAX_ALGO_SIMT, s);
+}
+
+// ================================================================ fp16 twins
+void pax_gemm_f16_launch(const __half* A, const __half* B, __half* C, int m, int n, int k, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F16, PAX_EPI_NONE, 1.f, nullptr, nullptr, PAX_DT_F16, s,
+                "pax_gemm_f16_launch");
+}
+void pax_gemm_bias_f16_launch(const __half* A, const __half* B, __half* C, int m, int n, int k,
+                              const __half* bias, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F16, PAX_EPI_BIAS, 1.f, bias, nullptr, PAX_DT_F16, s,
+                "pax_gemm_bias_f16_launch");
+}
+void pax_gemm_bias_gelu_f16_launch(const __half* A, const __half* B, __half* C, int m, int n, int k,
+                                   const __half* bias, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F16, PAX_EPI_BIAS_GELU_TANH, 1.f, bias, nullptr, PAX_DT_F16, s,
+                "pax_gemm_bias_gelu_f16_launch");
+}
+void pax_gemm_bias_gelu_erf_f16_launch(const __half* A, const __half* B, __half* C, int m, int n, int k,
+                                       const __half* bias, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F16, PAX_EPI_BIAS_GELU_ERF, 1.f, bias, nullptr, PAX_DT_F16, s,
+                "pax_gemm_bias_gelu_erf_f16_launch");
+}
+void pax_gemm_residual_gelu_f16_launch(const __half* A, const __half* B, __half* C, int m, int n, int k,
+                                       const __half* residual, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F16, PAX_EPI_RESIDUAL_GELU_TANH, 1.f, nullptr, residual, PAX_DT_F16, s,
+                "pax_gemm_residual_gelu_f16_launch");
+}
+void pax_gemm_residual_gelu_erf_f16_launch(const __half* A, const __half* B, __half* C, int m, int n, int k,
+                                           const __half* residual, cudaStream_t s) {
+    gemm_simple(A, B, C, m, n, k, PAX_DT_F16, PAX_EPI_RESIDUAL_GELU_ERF, 1.f, nullptr, residual, PAX_DT_F16, s,
+                "pax_gemm_residual_gelu_erf_f16_launch");
+}
+
+// ================================================================ buffers
+int pax_validate_buffer(const pax_buffer_t* buf) {
+    if (!buf) {
+        fail(PAX_ERR_INVALID, "validate_buffer: NULL descriptor");
+        return 0;
+    }
+    if (!buf->base) {
+        fail(PAX_ERR_INVALID, "validate_buffer: NULL base pointer");
+        return 0;
+    }
+    if (buf->elem_size == 0) {
+        fail(PAX_ERR_INVALID, "validate_buffer: elem_size == 0");
+        return 0;
+    }
+    if (buf->ndim < 1 || buf->ndim > 3) {
+        fail(PAX_ERR_INVALID, "validate_buffer: ndim=%d out of [1,3]", buf->ndim);
+        return 0;
+    }
+    for (int d = 0; d < buf->ndim; ++d) {
+        if (buf->shape[d] <= 0) {
+            fail(PAX_ERR_INVALID, "validate_buffer: shape[%d]=%lld <= 0", d, (long long)buf->shape[d]);
+            return 0;
+        }
+        if (buf->stride[d] <= 0) {
+            fail(PAX_ERR_INVALID, "validate_buffer: stride[%d]=%lld <= 0", d, (long long)buf->stride[d]);
+            return 0;
+        }
+    }
+    if (buf->alignment && (reinterpret_cast<uintptr_t>(buf->base) % buf->alignment != 0)) {
+        fail(PAX_ERR_INVALID, "validate_buffer: base %p not aligned to %zu", buf->base, buf->alignment);
+        return 0;
+    }
+    set_status(PAX_OK);
+    return 1;
+}
+
+static pax_buffer_t make_buffer(int ndim, size_t d0, size_t d1, size_t elem, size_t align, pax_ownership_t own,
+                                cudaStream_t s) {
+    pax_buffer_t b;
+    memset(&b, 0, sizeof(b));
+    b.elem_size = elem;
+    b.ndim = ndim;
+    b.shape[0] = (int64_t)d0;
+    if (ndim == 1) {
+        b.stride[0] = 1;
+    } else {
+        b.shape[1] = (int64_t)d1;
+        b.stride[0] = (int64_t)d1;
+        b.stride[1] = 1;
+    }
+    b.alignment = align;
+    b.ownership = own;
+    b.stream = s;
+    return b;
+}
+
+pax_buffer_t pax_alloc_device_1d(size_t nelems, size_t elem_size, cudaStream_t stream) {
+    pax_buffer_t b = make_buffer(1, nelems, 0, elem_size, 256, PAX_DEVICE, stream);
+    if (cudaMalloc(&b.base, nelems * elem_size) != cudaSuccess) {
+        fail(PAX_ERR_ALLOC, "pax_alloc_device_1d: cudaMalloc failed (%zu bytes)", nelems * elem_size);
+        b.base = nullptr;
+    } else {
+        set_status(PAX_OK);
+    }
+    return b;
+}
+
+pax_buffer_t pax_alloc_device_2d(size_t rows, size_t cols, size_t elem_size, cudaStream_t stream) {
+    pax_buffer_t b = make_buffer(2, rows, cols, elem_size, 256, PAX_DEVICE, stream);
+    if (cudaMalloc(&b.base, rows * cols * elem_size) != cudaSuccess) {
+        fail(PAX_ERR_ALLOC, "pax_alloc_device_2d: cudaMalloc failed (%zu bytes)", rows * cols * elem_size);
+        b.base = nullptr;
+    } else {
+        set_status(PAX_OK);
+    }
+    return b;
+}
+
+pax_buffer_t pax_alloc_host_1d(size_t nelems, size_t elem_size, cudaStream_t stream) {
+    pax_buffer_t b = make_buffer(1, nelems, 0, elem_size, 64, PAX_HOST, stream);
+    if (cudaMallocHost(&b.base, nelems * elem_size) != cudaSuccess) {
+        fail(PAX_ERR_ALLOC, "pax_alloc_host_1d: cudaMallocHost failed");
+        b.base = nullptr;
+    } else {
+        set_status(PAX_OK);
+    }
+    return b;
+}
+
+pax_buffer_t pax_alloc_host_2d(size_t rows, size_t cols, size_t elem_size, cudaStream_t stream) {
+    pax_buffer_t b = make_buffer(2, rows, cols, elem_size, 64, PAX_HOST, stream);
+    if (cudaMallocHost(&b.base, rows * cols * elem_size) != cudaSuccess) {
+        fail(PAX_ERR_ALLOC, "pax_alloc_host_2d: cudaMallocHost failed");
+        b.base = nullptr;
+    } else {
+        set_status(PAX_OK);
+    }
+    return b;
+}
+
+void pax_free_device(pax_buffer_t* buf) {
+    if (buf && buf->base) {
+        cudaFree(buf->base);
+        buf->base = nullptr;
+    }
+}
+
+void pax_free_host(pax_buffer_t* buf) {
+    if (buf && buf->base) {
+        cudaFreeHost(buf->base);
+        buf->base = nullptr;
+    }
+}
+
+// ============================================================ dispatchers
+// The reference reads m = A.shape[0], k = A.shape[1], n = B.shape[1] and
+// ignores strides (src/host_bridge.c:317-321); row strides are honoured here.
+static bool buffers_to_desc(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, pax_gemm_desc_t* d,
+                            const char* who) {
+    if (!pax_validate_buffer(A) || !pax_validate_buffer(B) || !pax_validate_buffer(C)) return false;
+    memset(d, 0, sizeof(*d));
+    d->A = A->base;
+    d->B = B->base;
+    d->C = C->base;
+    d->M = A->shape[0];
+    d->K = A->shape[1];
+    d->N = B->shape[1];
+    d->lda = (A->ndim >= 2 && A->stride[1] == 1) ? A->stride[0] : 0;
+    d->ldb = (B->ndim >= 2 && B->stride[1] == 1) ? B->stride[0] : 0;
+    d->ldc = (C->ndim >= 2 && C->stride[1] == 1) ? C->stride[0] : 0;
+    if (C->elem_size == 4) {
+        d->c_dtype = PAX_DT_F32;
+    } else if (C->elem_size == 2) {
+        d->c_dtype = PAX_DT_F16;
+    } else {
+        fail(PAX_ERR_INVALID, "%s: C elem_size %zu is neither 4 (fp32) nor 2 (fp16)", who, C->elem_size);
+        return false;
+    }
+    if (A->elem_size != 2 || B->elem_size != 2) {
+        fail(PAX_ERR_INVALID, "%s: A and B must be fp16 (elem_size 2)", who);
+        return false;
+    }
+    d->alpha = 1.f;
+    d->algo = PAX_ALGO_AUTO;
+    return true;
+}
+
+static void dispatch_plain(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, cudaStream_t s, const char* who) {
+    pax_gemm_desc_t d;
+    if (!buffers_to_desc(A, B, C, &d, who)) return;
+    d.epilogue = PAX_EPI_NONE;
+    pax_gemm_ex(&d, s);
+}
+
+void pax_dispatch_wmma_gemm(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, cudaStream_t s) {
+    dispatch_plain(A, B, C, s, "pax_dispatch_wmma_gemm");
+}
+void pax_dispatch_ptx_gemm(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, cudaStream_t s) {
+    dispatch_plain(A, B, C, s, "pax_dispatch_ptx_gemm");
+}
+void pax_dispatch_pipeline_gemm(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, cudaStream_t s) {
+    dispatch_plain(A, B, C, s, "pax_dispatch_pipeline_gemm");
+}
+
+void pax_dispatch_bias_gelu(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, const __half* bias,
+                            cudaStream_t s) {
+    pax_gemm_desc_t d;
+    if (!buffers_to_desc(A, B, C, &d, "pax_dispatch_bias_gelu")) return;
+    if (!bias) {
+        fail(PAX_ERR_INVALID, "pax_dispatch_bias_gelu: NULL bias");
+        return;
+    }
+    d.epilogue = PAX_EPI_BIAS_GELU_TANH;
+    d.bias = bias;
+    pax_gemm_ex(&d, s);
+}
+
+void pax_dispatch_residual_gelu(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, const float* residual,
+                                cudaStream_t s) {
+    pax_gemm_desc_t d;
+    if (!buffers_to_desc(A, B, C, &d, "pax_dispatch_residual_gelu")) return;
+    if (!residual) {
+        fail(PAX_ERR_INVALID, "pax_dispatch_residual_gelu: NULL residual");
+        return;
+    }
+    d.epilogue = PAX_EPI_RESIDUAL_GELU_TANH;
+    d.residual = residual;
+    d.residual_dtype = PAX_DT_F32;
+    pax_gemm_ex(&d, s);
+}
+
+void pax_dispatch_scale_bias_gelu(pax_buffer_t* A, pax_buffer_t* B, pax_buffer_t* C, float alpha,
+                                  const __half* bias, cudaStream_t s) {
+    pax_gemm_desc_t d;
+    if (!buffers_to_desc(A, B, C, &d, "pax_dispatch_scale_bias_gelu")) return;
+    if (!bias) {
+        fail(PAX_ERR_INVALID, "pax_dispatch_scale_bias_gelu: NULL bias");
+        return;
+    }
+    d.epilogue = PAX_EPI_BIAS_GELU_TANH;
+    d.alpha = alpha;
+    d.bias = bias;
+    pax_gemm_ex(&d, s);
+}
+
+// ============================================================ verification
+void cpu_gemm_ref(const float* A, const float* B, float* C, int m, int n, int k) {
+    for (int i = 0; i < m; ++i) {
+        const float* a = A + (size_t)i * k;
+        for (int j = 0; j < n; ++j) {
+            float s = 0.f;
+            for (int l = 0; l < k; ++l) s += a[l] * B[(size_t)l * n + j];
+            C[(size_t)i * n + j] = s;
+        }
+    }
+}
+
+int pax_verify_gemm(const float* C_gpu, const float* C_ref, int m, int n, float tol) {
+    float worst = 0.f;
+    long long at = 0;
+    const long long total = (long long)m * n;
+    for (long long i = 0; i < total; ++i) {
+        const float e = fabsf(C_gpu[i] - C_ref[i]) / (fabsf(C_ref[i]) + 1e-8f);
+        if (e > worst) {
+            worst = e;
+            at = i;
+        }
+    }
+    if (worst <= tol) {
+        printf("[PAX] PASS  max_rel_err = %.6e  (tol = %.6e)\n", (double)worst, (double)tol);
+        return 1;
+    }
+    printf("[PAX] FAIL  max_rel_err = %.6e  (tol = %.6e)  at index %lld  gpu=%.6f  ref=%.6f\n", (double)worst,
+           (double)tol, at, (double)C_gpu[at], (double)C_ref[at]);
+    return 0;
+}
+
+// ================================================================ bench
+static struct {
+    bool ready = false;
+    int m = 0, n = 0, k = 0;
+    cudaStream_t stream = nullptr;
+    __half *A = nullptr, *B = nullptr, *bias = nullptr, *res16 = nullptr, *C16 = nullptr;
+    float *C32 = nullptr, *res32 = nullptr;
+} g_bench;
+
+void pax_bench_teardown(void) {
+    cudaFree(g_bench.A);
+    cudaFree(g_bench.B);
+    cudaFree(g_bench.bias);
+    cudaFree(g_bench.res16);
+    cudaFree(g_bench.C16);
+    cudaFree(g_bench.C32);
+    cudaFree(g_bench.res32);
+    g_bench.A = g_bench.B = g_bench.bias = g_bench.res16 = g_bench.C16 = nullptr;
+    g_bench.C32 = g_bench.res32 = nullptr;
+    g_bench.ready = false;
+}
+
+int pax_bench_setup(int m, int n, int k, cudaStream_t stream) {
+    pax_bench_teardown();
+    if (m <= 0 || n <= 0 || k <= 0) {
+        fail(PAX_ERR_INVALID, "pax_bench_setup: bad shape");
+        return 0;
+    }
+    const size_t mk = (size_t)m * k, kn = (size_t)k * n, mn = (size_t)m * n;
+    bool ok = cudaMalloc(&g_bench.A, mk * 2) == cudaSuccess && cudaMalloc(&g_bench.B, kn * 2) == cudaSuccess &&
+              cudaMalloc(&g_bench.bias, (size_t)n * 2) == cudaSuccess &&
+              cudaMalloc(&g_bench.res16, mn * 2) == cudaSuccess && cudaMalloc(&g_bench.C16, mn * 2) == cudaSuccess &&
+              cudaMalloc(&g_bench.C32, mn * 4) == cudaSuccess && cudaMalloc(&g_bench.res32, mn * 4) == cudaSuccess;
+    if (!ok) {
+        pax_bench_teardown();
+        fail(PAX_ERR_ALLOC, "pax_bench_setup: allocation failed");
+        return 0;
+    }
+    fill_uniform_f16(g_bench.A, (long long)mk, 1, -1.f, 1.f, stream);
+    fill_uniform_f16(g_bench.B, (long long)kn, 2, -1.f, 1.f, stream);
+    fill_uniform_f16(g_bench.bias, n, 3, -1.f, 1.f, stream);
+    fill_uniform_f16(g_bench.res16, (long long)mn, 4, -1.f, 1.f, stream);
+    cudaMemsetAsync(g_bench.res32, 0, mn * 4, stream);
+    g_bench.m = m;
+    g_bench.n = n;
+    g_bench.k = k;
+    g_bench.stream = stream;
+    g_bench.ready = cudaStreamSynchronize(stream) == cudaSuccess;
+    return g_bench.ready ? 1 : 0;
+}
+
+typedef void (*bench_fn)(cudaStream_t);
+
+static void b_wmma(cudaStream_t s) {
+    pax_gemm_wmma_launch(g_bench.A, g_bench.B, g_bench.C32, g_bench.m, g_bench.n, g_bench.k, s);
+}
+static void b_ptx(cudaStream_t s) {
+    pax_gemm_ptx_launch(g_bench.A, g_bench.B, g_bench.C32, g_bench.m, g_bench.n, g_bench.k, s);
+}
+static void b_pipe(cudaStream_t s) {
+    pax_gemm_pipeline_launch(g_bench.A, g_bench.B, g_bench.C32, g_bench.m, g_bench.n, g_bench.k, s);
+}
+static void b_bias_gelu(cudaStream_t s) {
+    pax_gemm_bias_gelu_launch(g_bench.A, g_bench.B, g_bench.C32, g_bench.m, g_bench.n, g_bench.k, g_bench.bias, s);
+}
+static void b_res_gelu(cudaStream_t s) {
+    pax_gemm_residual_gelu_launch(g_bench.A, g_bench.B, g_bench.C32, g_bench.m, g_bench.n, g_bench.k,
+                                  g_bench.res32, s);
+}
+static void b_bias_gelu_f16(cudaStream_t s) {
+    pax_gemm_bias_gelu_f16_launch(g_bench.A, g_bench.B, g_bench.C16, g_bench.m, g_bench.n, g_bench.k, g_bench.bias,
+                                  s);
+}
+static void b_res_gelu_erf_f16(cudaStream_t s) {
+    pax_gemm_residual_gelu_erf_f16_launch(g_bench.A, g_bench.B, g_bench.C16, g_bench.m, g_bench.n, g_bench.k,
+                                          g_bench.res16, s);
+}
+
+static double time_variant(bench_fn fn, int iters, cudaStream_t s) {
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    fn(s);  // warm-up
+    cudaStreamSynchronize(s);
+    cudaEventRecord(e0, s);
+    for (int i = 0; i < iters; ++i) fn(s);
+    cudaEventRecord(e1, s);
+    cudaEventSynchronize(e1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return (double)ms / (iters > 0 ? iters : 1);
+}
+
+void pax_bench_all(int iters) {
+    if (!g_bench.ready) {
+        fail(PAX_ERR_INVALID, "pax_bench_all: call pax_bench_setup first");
+        return;
+    }
+    printf("\n[PAX] Benchmark  m=%d  n=%d  k=%d  iters=%d\n", g_bench.m, g_bench.n, g_bench.k, iters);
+    printf("%-28s  %10s  %10s\n", "Kernel", "ms/iter", "TFLOPS");
+    const double flops = 2.0 * g_bench.m * (double)g_bench.n * (double)g_bench.k;
+    struct {
+        const char* name;
+        bench_fn fn;
+    } variants[] = {
+        {"wmma", b_wmma},         {"ptx", b_ptx},
+        {"pipeline", b_pipe},     {"bias_gelu", b_bias_gelu},
+        {"residual_gelu", b_res_gelu}, {"bias_gelu_f16", b_bias_gelu_f16},
+        {"residual_gelu_erf_f16", b_res_gelu_erf_f16},
+    };
+    for (auto& v : variants) {
+        const double ms = time_variant(v.fn, iters, g_bench.stream);
+        printf("%-28s  %10.4f  %10.3f\n", v.name, ms, flops / (ms * 1e9));
+    }
+    printf("\n");
+}
+
+}  // extern "C"

@@ -1,0 +1,59 @@
+// internal.h -- host-side interface between the C-ABI layer (host_bridge.cpp)
+// and the kernel translation units.  Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/pax.h"
+#include "params.h"
+
+namespace pax {
+
+// A validated, normalised GEMM problem: C[M][ldc] = epi(A[M][lda] . B[K][ldb]).
+struct Problem {
+    const __half* A;
+    const __half* B;
+    void* C;
+    long long M, N, K;
+    long long lda, ldb, ldc;
+    bool c_f16;
+    EpiParams epi;
+};
+
+// Per-device facts the launchers need (cached).
+int device_sm_count(int dev);
+int current_device();
+
+// TMA-based kernels need 16-byte aligned bases and row pitches.
+bool tma_compatible(const Problem& p);
+
+// Launchers.  Each returns PAX_OK or an error status; none synchronises.
+pax_status_t launch_tc(const Problem& p, int bn, cudaStream_t stream);
+pax_status_t launch_simt(const Problem& p, cudaStream_t stream);
+// Skinny kernel: `ws` holds grid*2*MP*128 fp32 partial sums and `counters`
+// one int per 128-column tile, zero before the launch (the kernel leaves
+// them zero again).  skinny_geometry gives the grid and both sizes.
+void skinny_geometry(long long M, long long N, long long K, int sms, int* grid, size_t* ws_bytes,
+                     size_t* counter_bytes);
+pax_status_t launch_skinny_ws(const Problem& p, int grid, float* ws, int* counters, cudaStream_t stream);
+
+// Dynamic shared memory of the tcgen05 kernel for a tile width / output type.
+size_t tc_smem_bytes(int bn, bool c_f16);
+// Tile width launch_tc picks for a problem when none is forced.
+int tc_pick_bn(long long M, long long N, int sms);
+// Largest M the skinny kernel accepts.
+constexpr long long kSkinnyMaxM = 64;
+
+// Read and clear the device error word of each kernel translation unit on
+// the current device.
+int read_clear_device_error_tc();
+int read_clear_device_error_skinny();
+
+// Fill a device fp16 buffer with a counter-hash uniform[lo,hi) pattern
+// (bench state only).
+pax_status_t fill_uniform_f16(__half* p, long long n, unsigned long long seed, float lo, float hi,
+                              cudaStream_t stream);
+
+}  // namespace pax

@@ -1,0 +1,28 @@
+// params.h -- epilogue parameter block shared by host code and kernels.
+// Plain C++ (no device code) so the C-ABI layer can build it.
+#pragma once
+
+#include <cuda_fp16.h>
+
+namespace pax {
+
+enum EpiFlags : int {
+    EPI_BIAS      = 1 << 0,  // add fp16 bias[j]
+    EPI_RES       = 1 << 1,  // add residual R[i][j]
+    EPI_RES_F32   = 1 << 2,  // residual is fp32 (else fp16)
+    EPI_GELU_TANH = 1 << 3,
+    EPI_GELU_ERF  = 1 << 4,
+    EPI_SCALE     = 1 << 5,  // multiply by alpha first
+    EPI_BIAS_VEC  = 1 << 6,  // bias pointer 16-byte aligned (vector loads allowed)
+    EPI_RES_VEC   = 1 << 7   // residual base and row pitch 16-byte aligned
+};
+
+struct EpiParams {
+    const __half* bias;     // [N]
+    const void* residual;   // [M][ld_res]
+    long long ld_res;       // elements
+    float alpha;
+    int flags;
+};
+
+}  // namespace pax

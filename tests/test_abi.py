@@ -1,0 +1,190 @@
+"""The C ABI (include/pax.h) on the host, without a GPU: exports, struct
+layouts, argument checking, algorithm selection, and the host-side
+verification functions the bridge mirrors from src/host_bridge.c."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import oracle
+import pax_b200
+from pax_b200 import Algo, GemmDesc, PaxBuffer, lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "pax.h")
+
+
+def declared_functions() -> list[str]:
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^[A-Za-z_][\w\s\*]*?\b(\w+)\s*\([^;{]*\)\s*;", src, flags=re.M)
+    return sorted(set(n for n in names if n not in ("if", "while")))
+
+
+def test_header_declares_the_reference_surface():
+    names = set(declared_functions())
+    for ref_name in ["pax_gemm_wmma_launch", "pax_gemm_ptx_launch", "pax_gemm_ptx_smem_bytes",
+                     "pax_gemm_pipeline_launch", "pax_gemm_pipeline_smem_bytes", "pax_gemm_bias_gelu_launch",
+                     "pax_gemm_residual_gelu_launch", "pax_gemm_scale_bias_gelu_launch",
+                     "pax_gemm_tma_cluster_launch", "pax_gemm_tma_smem_bytes", "pax_validate_buffer",
+                     "pax_alloc_device_1d", "pax_alloc_device_2d", "pax_alloc_host_1d", "pax_alloc_host_2d",
+                     "pax_free_device", "pax_free_host", "pax_dispatch_wmma_gemm", "pax_dispatch_ptx_gemm",
+                     "pax_dispatch_pipeline_gemm", "pax_dispatch_bias_gelu", "pax_dispatch_residual_gelu",
+                     "cpu_gemm_ref", "pax_verify_gemm", "pax_bench_all"]:
+        assert ref_name in names, ref_name
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", pax_b200.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(line.split()[-1] for line in out.splitlines() if " T " in line)
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, missing
+    for n in declared_functions():  # and ctypes can bind each of them
+        getattr(lib, n)
+
+
+def test_header_compiles_as_c(tmp_path):
+    c = tmp_path / "use.c"
+    c.write_text('#include "pax.h"\nint main(void){ pax_buffer_t b; (void)b; return (int)sizeof(pax_gemm_desc_t) > 0 ? 0 : 1; }\n')
+    subprocess.run(["gcc", "-std=c99", "-I", os.path.join(ROOT, "include"), "-I", "/usr/local/cuda/include",
+                    "-c", str(c), "-o", str(tmp_path / "use.o")], check=True)
+
+
+def test_struct_layouts_match():
+    assert lib.pax_sizeof_buffer() == ctypes.sizeof(PaxBuffer) == 96
+    assert lib.pax_sizeof_gemm_desc() == ctypes.sizeof(GemmDesc)
+
+
+def _host_buffer(arr: np.ndarray) -> PaxBuffer:
+    b = PaxBuffer()
+    b.base = arr.ctypes.data
+    b.elem_size = arr.itemsize
+    b.ndim = arr.ndim
+    for i in range(arr.ndim):
+        b.shape[i] = arr.shape[i]
+        b.stride[i] = arr.strides[i] // arr.itemsize
+    b.alignment = 0
+    return b
+
+
+def test_validate_buffer_semantics():
+    a = np.zeros((4, 8), np.float32)
+    b = _host_buffer(a)
+    assert lib.pax_validate_buffer(ctypes.byref(b)) == 1
+    assert lib.pax_validate_buffer(None) == 0
+    bad = _host_buffer(a)
+    bad.base = None
+    assert lib.pax_validate_buffer(ctypes.byref(bad)) == 0
+    bad = _host_buffer(a)
+    bad.ndim = 4
+    assert lib.pax_validate_buffer(ctypes.byref(bad)) == 0
+    bad = _host_buffer(a)
+    bad.shape[1] = 0
+    assert lib.pax_validate_buffer(ctypes.byref(bad)) == 0
+    bad = _host_buffer(a)
+    bad.stride[0] = -1
+    assert lib.pax_validate_buffer(ctypes.byref(bad)) == 0
+    bad = _host_buffer(a)
+    bad.elem_size = 0
+    assert lib.pax_validate_buffer(ctypes.byref(bad)) == 0
+    odd = _host_buffer(a)
+    odd.base = a.ctypes.data + 4
+    odd.alignment = 8
+    assert lib.pax_validate_buffer(ctypes.byref(odd)) == (1 if (a.ctypes.data + 4) % 8 == 0 else 0)
+
+
+def test_cpu_gemm_ref_matches_reference_build(rng):
+    A = rng.uniform(-1, 1, (33, 65)).astype(np.float16).astype(np.float32)
+    B = rng.uniform(-1, 1, (65, 47)).astype(np.float16).astype(np.float32)
+    C = np.empty((33, 47), np.float32)
+    lib.cpu_gemm_ref(A.ctypes.data, B.ctypes.data, C.ctypes.data, 33, 47, 65)
+    assert np.array_equal(C.view(np.uint32), oracle.cpu_gemm_ref(A, B).view(np.uint32))
+    if oracle.ref_lib() is not None:
+        assert np.array_equal(C.view(np.uint32), oracle.reference_cpu_gemm_ref(A, B).view(np.uint32))
+
+
+def test_verify_gemm_matches_reference_decisions():
+    d = np.load(os.path.join(ROOT, "tests", "golden", "verify_decisions.npz"))
+    ref = np.ascontiguousarray(d["C_ref"])
+    for i in range(d["C_gpu"].shape[0]):
+        g = np.ascontiguousarray(d["C_gpu"][i])
+        for j, tol in enumerate(d["tols"]):
+            got = lib.pax_verify_gemm(g.ctypes.data, ref.ctypes.data, ref.shape[0], ref.shape[1], float(tol))
+            assert got == d["decisions"][i, j]
+
+
+def _desc(M=256, N=256, K=256, ptr=0x10000, **kw) -> GemmDesc:
+    d = GemmDesc()
+    d.A = d.B = d.C = ptr
+    d.M, d.N, d.K = M, N, K
+    d.alpha = 1.0
+    d.c_dtype = kw.get("c_dtype", 1)
+    d.epilogue = kw.get("epilogue", 0)
+    d.bias = kw.get("bias", None)
+    d.residual = kw.get("residual", None)
+    d.lda = kw.get("lda", 0)
+    return d
+
+
+def test_gemm_ex_rejects_bad_arguments_before_touching_the_device():
+    assert lib.pax_gemm_ex(None, None) == pax_b200.Status.INVALID
+    d = _desc(M=-1)
+    assert lib.pax_gemm_ex(ctypes.byref(d), None) == pax_b200.Status.INVALID
+    d = _desc(epilogue=99)
+    assert lib.pax_gemm_ex(ctypes.byref(d), None) == pax_b200.Status.INVALID
+    d = _desc(epilogue=2)  # bias epilogue, NULL bias
+    assert lib.pax_gemm_ex(ctypes.byref(d), None) == pax_b200.Status.INVALID
+    d = _desc(epilogue=4)  # residual epilogue, NULL residual
+    assert lib.pax_gemm_ex(ctypes.byref(d), None) == pax_b200.Status.INVALID
+    d = _desc(lda=100)  # lda < K
+    assert lib.pax_gemm_ex(ctypes.byref(d), None) == pax_b200.Status.INVALID
+    d = _desc()
+    d.C = None
+    assert lib.pax_gemm_ex(ctypes.byref(d), None) == pax_b200.Status.INVALID
+    assert lib.pax_last_error() == pax_b200.Status.INVALID
+    d = _desc(M=0)  # empty output: nothing to do, no device needed
+    assert lib.pax_gemm_ex(ctypes.byref(d), None) == pax_b200.Status.OK
+
+
+def test_algorithm_selection():
+    sel = lambda d: Algo(lib.pax_gemm_select_algo(ctypes.byref(d)))  # noqa: E731
+    assert sel(_desc(4096, 4096, 4096)) == Algo.TC
+    assert sel(_desc(16, 16384, 4096)) == Algo.SKINNY
+    assert sel(_desc(64, 16384, 4096)) == Algo.SKINNY
+    assert sel(_desc(65, 16384, 4096)) == Algo.TC
+    assert sel(_desc(128, 129, 256)) == Algo.SIMT      # fp16 row pitch not 16-byte aligned
+    assert sel(_desc(128, 128, 100)) == Algo.SIMT      # K pitch 200 bytes
+    assert sel(_desc(128, 128, 0)) == Algo.SIMT        # K == 0: epilogue of zero
+    assert sel(_desc(128, 128, 128, ptr=0x10008)) == Algo.SIMT  # base not 16-byte aligned
+    d = _desc(128, 132, 128, c_dtype=0)  # fp32 C pitch 528 B ok, but B pitch 264 B is not
+    assert sel(d) == Algo.SIMT
+
+
+def test_status_strings_and_version():
+    for s in pax_b200.Status:
+        assert lib.pax_status_string(int(s))
+    assert b"sm_100a" in lib.pax_version()
+
+
+def test_smem_queries_fit_the_part():
+    for f in (lib.pax_gemm_ptx_smem_bytes, lib.pax_gemm_pipeline_smem_bytes, lib.pax_gemm_tma_smem_bytes):
+        assert 0 < f() <= 232448
+
+
+def test_dispatch_rejects_invalid_buffers_without_gpu(capfd):
+    a = np.zeros((4, 8), np.float16)
+    good = _host_buffer(a)
+    bad = _host_buffer(a)
+    bad.base = None
+    lib.pax_dispatch_wmma_gemm(ctypes.byref(bad), ctypes.byref(good), ctypes.byref(good), None)
+    assert lib.pax_last_error() == pax_b200.Status.INVALID
+    lib.pax_dispatch_bias_gelu(ctypes.byref(good), ctypes.byref(good), ctypes.byref(good), None, None)
+    assert lib.pax_last_error() == pax_b200.Status.INVALID
+    err = capfd.readouterr().err
+    assert "[PAX]" in err and "NULL" in err

@@ -1,0 +1,283 @@
+"""CUDA kernels vs the oracle on seeded inputs, through the C ABI.
+
+Every case runs libpax_b200.so (pax_gemm_ex or a reference-named launcher)
+and compares with oracle.gemm: fp32-accumulated products of the same fp16
+inputs with the reference's epilogue math.
+"""
+from __future__ import annotations
+
+import ctypes
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import pax_b200
+from _helpers import check, inputs, run_gemm, to_dev
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def stream_ptr():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+# ---------------------------------------------------------------- tcgen05 core
+@pytest.mark.parametrize("bn", [256, 128])
+@pytest.mark.parametrize("shape", [(128, 256, 64), (256, 512, 128), (384, 768, 1024)])
+@pytest.mark.parametrize("out", [np.float32, np.float16])
+def test_tc_plain(cuda, rng, monkeypatch, bn, shape, out):
+    monkeypatch.setenv("PAX_TC_BN", str(bn))
+    M, N, K = shape
+    A, B = inputs(rng, M, N, K)
+    got = run_gemm(A, B, cuda, out_dtype=out, algo="tc")
+    check(got, oracle.gemm(A, B, out_dtype=out), out)
+
+
+@pytest.mark.parametrize("shape", [(300, 520, 200), (129, 264, 72), (1000, 8, 8), (65, 1032, 136), (77, 40, 4104)])
+@pytest.mark.parametrize("out", [np.float32, np.float16])
+def test_tc_ragged_edges(cuda, rng, shape, out):
+    M, N, K = shape
+    A, B = inputs(rng, M, N, K)
+    got = run_gemm(A, B, cuda, out_dtype=out, algo="tc")
+    check(got, oracle.gemm(A, B, out_dtype=out), out)
+
+
+EPIS = ["none", "bias", "bias_gelu_tanh", "bias_gelu_erf", "residual_gelu_tanh", "residual_gelu_erf", "gelu_tanh",
+        "gelu_erf", "residual"]
+
+
+@pytest.mark.parametrize("epi", EPIS)
+@pytest.mark.parametrize("out", [np.float32, np.float16])
+@pytest.mark.parametrize("res_dtype", [np.float32, np.float16])
+def test_tc_epilogues(cuda, rng, epi, out, res_dtype):
+    if "residual" not in epi and res_dtype == np.float16:
+        pytest.skip("residual dtype irrelevant")
+    M, N, K = 256, 520, 320
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    res = rng.standard_normal((M, N)).astype(res_dtype)
+    got = run_gemm(A, B, cuda, epi=epi, out_dtype=out, bias=bias if "bias" in epi else None,
+                   residual=res if "residual" in epi else None, algo="tc")
+    ref = oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out)
+    check(got, ref, out)
+
+
+@pytest.mark.parametrize("algo", ["tc", "skinny", "simt"])
+def test_scale_bias_gelu(cuda, rng, algo):
+    M = 48 if algo == "skinny" else 200
+    A, B = inputs(rng, M, 264, 192)
+    bias = rng.standard_normal(264).astype(np.float16)
+    got = run_gemm(A, B, cuda, epi="bias_gelu_tanh", bias=bias, alpha=0.37, out_dtype=np.float32, algo=algo)
+    check(got, oracle.gemm(A, B, epi="bias_gelu_tanh", bias=bias, alpha=0.37), np.float32)
+
+
+# ---------------------------------------------------------------- skinny
+@pytest.mark.parametrize("M", [1, 8, 16, 17, 33, 48, 64])
+@pytest.mark.parametrize("NK", [(128, 64), (1000, 320), (4096, 4096), (384, 136)])
+def test_skinny(cuda, rng, M, NK):
+    N, K = NK
+    A, B = inputs(rng, M, N, K, dist="normal")
+    bias = rng.standard_normal(N).astype(np.float16)
+    got = run_gemm(A, B, cuda, epi="bias", bias=bias, out_dtype=np.float16, algo="skinny")
+    check(got, oracle.gemm(A, B, epi="bias", bias=bias, out_dtype=np.float16), np.float16)
+
+
+@pytest.mark.parametrize("epi", ["none", "bias_gelu_erf", "residual_gelu_tanh"])
+@pytest.mark.parametrize("out", [np.float32, np.float16])
+def test_skinny_epilogues(cuda, rng, epi, out):
+    M, N, K = 16, 2048, 1024
+    A, B = inputs(rng, M, N, K, dist="normal")
+    bias = rng.standard_normal(N).astype(np.float16)
+    res = rng.standard_normal((M, N)).astype(np.float16)
+    got = run_gemm(A, B, cuda, epi=epi, bias=bias, residual=res, out_dtype=out, algo="skinny")
+    check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
+
+
+# ---------------------------------------------------------------- SIMT
+@pytest.mark.parametrize("shape", [(1, 1, 1), (17, 17, 17), (127, 33, 129), (5, 300, 7), (64, 64, 0)])
+@pytest.mark.parametrize("epi", ["none", "bias_gelu_tanh", "residual_gelu_erf"])
+def test_simt_unaligned(cuda, rng, shape, epi):
+    M, N, K = shape
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    got = run_gemm(A, B, cuda, epi=epi, bias=bias, residual=res, out_dtype=np.float32)
+    assert pax_b200.select_algo(to_dev(A, cuda), to_dev(B, cuda),
+                                torch.empty((M, N), dtype=torch.float32, device=cuda)) == pax_b200.Algo.SIMT
+    check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res), np.float32)
+
+
+# ---------------------------------------------------------------- exactness
+@pytest.mark.parametrize("algo,M", [("tc", 256), ("skinny", 16), ("simt", 256)])
+def test_integer_inputs_bit_exact(cuda, rng, algo, M):
+    A = rng.integers(-3, 4, (M, 512)).astype(np.float16)
+    B = rng.integers(-3, 4, (512, 384)).astype(np.float16)
+    got = run_gemm(A, B, cuda, out_dtype=np.float32, algo=algo)
+    exact = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.float32)
+    assert np.array_equal(got, exact)
+
+
+GOLDEN = sorted(glob.glob(os.path.join(ROOT, "tests", "golden", "gemm_*.npz")))
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=lambda p: os.path.basename(p)[5:-4])
+def test_golden_through_reference_launcher(cuda, path):
+    d = np.load(path)
+    A, B, C = d["A"], d["B"], d["C"]
+    M, K = A.shape
+    N = B.shape[1]
+    tA, tB = to_dev(A, cuda), to_dev(B, cuda)
+    tC = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    pax_b200.lib.pax_gemm_wmma_launch(tA.data_ptr(), tB.data_ptr(), tC.data_ptr(), M, N, K, stream_ptr())
+    torch.cuda.synchronize()
+    got = tC.cpu().numpy()
+    name = os.path.basename(path)
+    if any(s in name for s in ("int_kat", "identity", "permutation")):
+        assert np.array_equal(got, C)
+    else:
+        check(got, C, np.float32)
+
+
+def test_reference_wmma_kernel_agrees(cuda, rng):
+    """The reference's own sm_86 WMMA kernel, compiled for sm_100a from its
+    source (oracle/_ref), on a shape it handles (M, N multiples of 16, K of 8)."""
+    path = oracle.REF_WMMA_PATH
+    if not os.path.exists(path):
+        pytest.skip("oracle/_ref/libpaxref_wmma.so not built")
+    L = ctypes.CDLL(path)
+    L.pax_gemm_wmma_launch.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]
+    M, N, K = 256, 384, 512
+    A, B = inputs(rng, M, N, K)
+    tA, tB = to_dev(A, cuda), to_dev(B, cuda)
+    ref_out = torch.zeros((M, N), dtype=torch.float32, device=cuda)
+    L.pax_gemm_wmma_launch(tA.data_ptr(), tB.data_ptr(), ref_out.data_ptr(), M, N, K, stream_ptr())
+    ours = torch.zeros_like(ref_out)
+    pax_b200.lib.pax_gemm_wmma_launch(tA.data_ptr(), tB.data_ptr(), ours.data_ptr(), M, N, K, stream_ptr())
+    torch.cuda.synchronize()
+    check(ours.cpu().numpy(), ref_out.cpu().numpy(), np.float32)
+
+
+# ---------------------------------------------------------------- C ABI surface
+def test_reference_named_launchers(cuda, rng):
+    M, N, K = 256, 512, 256
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    res32 = rng.standard_normal((M, N)).astype(np.float32)
+    res16 = res32.astype(np.float16)
+    tA, tB, tb = to_dev(A, cuda), to_dev(B, cuda), to_dev(bias, cuda)
+    tr32, tr16 = to_dev(res32, cuda), to_dev(res16, cuda)
+    L = pax_b200.lib
+    s = stream_ptr()
+    c32 = lambda: torch.empty((M, N), dtype=torch.float32, device=cuda)  # noqa: E731
+    c16 = lambda: torch.empty((M, N), dtype=torch.float16, device=cuda)  # noqa: E731
+    cases = []
+    for name in ("pax_gemm_wmma_launch", "pax_gemm_ptx_launch", "pax_gemm_pipeline_launch"):
+        C = c32()
+        getattr(L, name)(tA.data_ptr(), tB.data_ptr(), C.data_ptr(), M, N, K, s)
+        cases.append((C, oracle.gemm(A, B), np.float32))
+    C = c32()
+    L.pax_gemm_tma_cluster_launch(tA.data_ptr(), tB.data_ptr(), C.data_ptr(), M, N, K, None, None, None, s)
+    cases.append((C, oracle.gemm(A, B), np.float32))
+    C = c32()
+    L.pax_gemm_bias_gelu_launch(tA.data_ptr(), tB.data_ptr(), C.data_ptr(), M, N, K, tb.data_ptr(), s)
+    cases.append((C, oracle.gemm(A, B, "bias_gelu_tanh", bias=bias), np.float32))
+    C = c32()
+    L.pax_gemm_residual_gelu_launch(tA.data_ptr(), tB.data_ptr(), C.data_ptr(), M, N, K, tr32.data_ptr(), s)
+    cases.append((C, oracle.gemm(A, B, "residual_gelu_tanh", residual=res32), np.float32))
+    C = c32()
+    L.pax_gemm_scale_bias_gelu_launch(tA.data_ptr(), tB.data_ptr(), C.data_ptr(), M, N, K, 0.25, tb.data_ptr(), s)
+    cases.append((C, oracle.gemm(A, B, "bias_gelu_tanh", alpha=0.25, bias=bias), np.float32))
+    C = c16()
+    L.pax_gemm_f16_launch(tA.data_ptr(), tB.data_ptr(), C.data_ptr(), M, N, K, s)
+    cases.append((C, oracle.gemm(A, B, out_dtype=np.float16), np.float16))
+    for name, epi in (("pax_gemm_bias_f16_launch", "bias"), ("pax_gemm_bias_gelu_f16_launch", "bias_gelu_tanh"),
+                      ("pax_gemm_bias_gelu_erf_f16_launch", "bias_gelu_erf")):
+        C = c16()
+        getattr(L, name)(tA.data_ptr(), tB.data_ptr(), C.data_ptr(), M, N, K, tb.data_ptr(), s)
+        cases.append((C, oracle.gemm(A, B, epi, bias=bias, out_dtype=np.float16), np.float16))
+    for name, epi in (("pax_gemm_residual_gelu_f16_launch", "residual_gelu_tanh"),
+                      ("pax_gemm_residual_gelu_erf_f16_launch", "residual_gelu_erf")):
+        C = c16()
+        getattr(L, name)(tA.data_ptr(), tB.data_ptr(), C.data_ptr(), M, N, K, tr16.data_ptr(), s)
+        cases.append((C, oracle.gemm(A, B, epi, residual=res16, out_dtype=np.float16), np.float16))
+    torch.cuda.synchronize()
+    for C, ref, dt in cases:
+        check(C.cpu().numpy(), ref, dt)
+    assert L.pax_last_error() == 0
+
+
+def test_dispatchers_with_library_buffers(cuda, rng):
+    """pax_alloc_device_2d + pax_dispatch_* as a reference caller uses them."""
+    L = pax_b200.lib
+    M, N, K = 192, 256, 128
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    s = stream_ptr()
+    bA = L.pax_alloc_device_2d(M, K, 2, s)
+    bB = L.pax_alloc_device_2d(K, N, 2, s)
+    bC = L.pax_alloc_device_2d(M, N, 4, s)
+    bBias = L.pax_alloc_device_1d(N, 2, s)
+    try:
+        assert bA.base and bB.base and bC.base and bBias.base
+        for buf, arr in ((bA, A), (bB, B), (bBias, bias)):
+            torch.cuda.cudart().cudaMemcpy(buf.base, arr.ctypes.data, arr.nbytes, 1)
+        L.pax_dispatch_bias_gelu(ctypes.byref(bA), ctypes.byref(bB), ctypes.byref(bC), bBias.base, s)
+        torch.cuda.synchronize()
+        out = np.empty((M, N), np.float32)
+        torch.cuda.cudart().cudaMemcpy(out.ctypes.data, bC.base, out.nbytes, 2)
+        check(out, oracle.gemm(A, B, "bias_gelu_tanh", bias=bias), np.float32)
+        L.pax_dispatch_pipeline_gemm(ctypes.byref(bA), ctypes.byref(bB), ctypes.byref(bC), s)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaMemcpy(out.ctypes.data, bC.base, out.nbytes, 2)
+        check(out, oracle.gemm(A, B), np.float32)
+    finally:
+        for b in (bA, bB, bC, bBias):
+            L.pax_free_device(ctypes.byref(b))
+
+
+def test_strided_operands(cuda, rng):
+    """Row pitches larger than the row (sub-matrix views) are honoured."""
+    M, N, K = 256, 384, 256
+    bigA = rng.uniform(-1, 1, (M, K + 64)).astype(np.float16)
+    bigB = rng.uniform(-1, 1, (K, N + 128)).astype(np.float16)
+    tA = to_dev(bigA, cuda)[:, 32:32 + K]
+    tB = to_dev(bigB, cuda)[:, 64:64 + N]
+    outbig = torch.zeros((M, N + 64), dtype=torch.float16, device=cuda)
+    C = outbig[:, :N]
+    pax_b200.gemm(tA, tB, out=C)
+    torch.cuda.synchronize()
+    check(C.cpu().numpy(), oracle.gemm(bigA[:, 32:32 + K].copy(), bigB[:, 64:64 + N].copy(), out_dtype=np.float16),
+          np.float16)
+    assert (outbig[:, N:] == 0).all()
+
+
+# ---------------------------------------------------------------- properties
+def test_gelu_bound_on_device(cuda, rng):
+    """|GeLU_tanh - GeLU_exact| <= 1e-3 |x| on the kernel's own fp32 values."""
+    M, N, K = 256, 512, 512
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    x = run_gemm(A, B, cuda, epi="bias", bias=bias, out_dtype=np.float32)
+    t = run_gemm(A, B, cuda, epi="bias_gelu_tanh", bias=bias, out_dtype=np.float32)
+    e = run_gemm(A, B, cuda, epi="bias_gelu_erf", bias=bias, out_dtype=np.float32)
+    assert (np.abs(t - e) <= 1e-3 * np.abs(x) + 1e-6).all()
+
+
+@pytest.mark.parametrize("algo,M", [("tc", 1024), ("skinny", 16)])
+def test_deterministic(cuda, rng, algo, M):
+    N, K = 4096, 2048
+    A, B = inputs(rng, M, N, K)
+    tA, tB = to_dev(A, cuda), to_dev(B, cuda)
+    c1 = pax_b200.gemm(tA, tB, algo=algo)
+    c2 = pax_b200.gemm(tA, tB, algo=algo)
+    torch.cuda.synchronize()
+    assert torch.equal(c1.view(torch.int16), c2.view(torch.int16))
+
+
+def test_no_device_errors_recorded(cuda):
+    assert pax_b200.device_error() == pax_b200.Status.OK
