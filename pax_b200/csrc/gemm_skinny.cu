@@ -293,6 +293,7 @@ __global__ void __launch_bounds__(192, 1)
         }
     }
 
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

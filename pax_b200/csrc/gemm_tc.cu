@@ -255,8 +255,9 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) {
-                    tma_store_2d(&tmC, smem_u32(stg + sb * Cfg::STG_BYTES), (int)col0, mb * Cfg::BM + q * 32);
+                const int row0 = mb * Cfg::BM + q * 32;
+                if (lane == 0 && col0 < p.N && row0 < p.M) {  // boxes wholly outside C are skipped
+                    tma_store_2d(&tmC, smem_u32(stg + sb * Cfg::STG_BYTES), (int)col0, row0);
                     bulk_commit();
                 }
                 sb ^= 1;
@@ -270,6 +271,7 @@ __global__ void __launch_bounds__(192, 1)
         __syncwarp();
     }
 
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
