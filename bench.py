@@ -51,7 +51,7 @@ L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="pax", choices=["pax", "reference"])
@@ -59,6 +59,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=0x5EED)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--epilogue", default=None, help="override the configuration's epilogue (diagnostics)")
     return ap.parse_args()
 
 
@@ -168,7 +169,8 @@ def workload_config(cfg, world, args):
         "epilogue": cfg["epi"],
         "inputs": cfg["dist"],
         "parallelism": f"N-split over {world} GPU(s)" + (" + NCCL all-gather of C" if args.gather else ""),
-        "l2": "flushed between steps (256 MiB write)",
+        "l2": "flushed between steps (256 MiB write, then 256 MiB read of another buffer)",
+        "timing": "CUDA events around each launch; all steps queued behind a device sleep (no host gaps)",
     }
 
 
@@ -188,7 +190,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                          "-lms", "50", "-i", str(self.idx)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -266,7 +268,10 @@ def run_pax(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.epilogue:
+        cfg["epi"] = args.epilogue
+        cfg["name"] += f" [epilogue overridden: {args.epilogue}]"
     M, N, K = cfg["M"], cfg["N"], cfg["K"]
     g = torch.Generator(device=dev)
     g.manual_seed(args.seed + 1000 * rank)
@@ -282,7 +287,19 @@ def run_pax(args):
     gathered = None
     if args.gather and world > 1:
         gathered = torch.empty((world, M, N), dtype=torch.float16, device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    # L2 flush between steps: write a buffer larger than L2, then read a second
+    # one so the dirty lines are written back before the timed launch rather
+    # than during it.
+    flush_w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    class _Flush:
+        @staticmethod
+        def zero_():
+            flush_w.zero_()
+            flush_r.sum()
+
+    flush = _Flush()
     kw = dict(epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None, residual=res, out=C)
 
     def step():
@@ -298,9 +315,20 @@ def run_pax(args):
         dist.barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # Host cost of enqueueing one step, so that the whole timed loop can be
+    # queued behind a device-side sleep: the GPU then runs the steps back to
+    # back and no host launch latency falls between a start and stop event.
+    t0 = time.perf_counter()
+    for _ in range(3):
+        flush.zero_()
+        step()
+    host_step = (time.perf_counter() - t0) / 3
+    torch.cuda.synchronize()
+    gate_s = min(2.0, 2.0 * host_step * args.steps + 0.01)
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
+    torch.cuda._sleep(int(gate_s * 2.0e9))  # ~cycles at up to 2 GHz
     for i in range(args.steps):
         flush.zero_()
         starts[i].record()

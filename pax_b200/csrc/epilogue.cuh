@@ -57,98 +57,137 @@ __device__ __forceinline__ void unpack_h8(const uint4& u, float* f) {
     }
 }
 
-// Residual values of one row chunk, fetched ahead of the TMEM read so that
-// their global-memory latency overlaps it.  Holds n fp32 or n fp16 values
-// (the fp16 case uses the first n/8 vectors).
-template <int n>
+// Residual values of one row chunk of n columns, fetched ahead of the TMEM
+// read so that their global-memory latency overlaps it.  RES: 0 = none,
+// 1 = fp16 residual (n/8 vectors), 2 = fp32 residual (n/4 vectors).
+template <int n, int RES>
 struct ResChunk {
-    uint4 u[n / 4];
+    static constexpr int V = RES == 1 ? n / 8 : RES == 2 ? n / 4 : 1;
+    uint4 u[V];
 };
 
-template <int n>
-__device__ __forceinline__ void res_prefetch(ResChunk<n>& rc, long long row, long long col0, long long M,
+template <int n, int RES>
+__device__ __forceinline__ void res_prefetch(ResChunk<n, RES>& rc, long long row, long long col0, long long M,
                                              long long N, const EpiParams& ep) {
-    const int flags = ep.flags;
-    if (!(flags & EPI_RES)) return;
-#pragma unroll
-    for (int i = 0; i < n / 4; ++i) rc.u[i] = make_uint4(0u, 0u, 0u, 0u);
-    if (row >= M) return;
-    const bool full = (flags & EPI_RES_VEC) && col0 + n <= N;
-    if (flags & EPI_RES_F32) {
-        const float* rp = static_cast<const float*>(ep.residual) + row * ep.ld_res + col0;
-        if (full) {
-#pragma unroll
-            for (int i = 0; i < n / 4; ++i) rc.u[i] = ld_nc_v4(rp + 4 * i);
-        } else {
-#pragma unroll
-            for (int i = 0; i < n / 4; ++i) {
-                float x[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) x[e] = (col0 + 4 * i + e < N) ? rp[4 * i + e] : 0.f;
-                rc.u[i] = make_uint4(__float_as_uint(x[0]), __float_as_uint(x[1]), __float_as_uint(x[2]),
-                                     __float_as_uint(x[3]));
-            }
-        }
+    if constexpr (RES == 0) {
+        return;
     } else {
-        const __half* rp = static_cast<const __half*>(ep.residual) + row * ep.ld_res + col0;
-        if (full) {
 #pragma unroll
-            for (int i = 0; i < n / 8; ++i) rc.u[i] = ld_nc_v4(rp + 8 * i);
-        } else {
+        for (int i = 0; i < ResChunk<n, RES>::V; ++i) rc.u[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (row >= M) return;
+        const bool full = (ep.flags & EPI_RES_VEC) && col0 + n <= N;
+        if constexpr (RES == 2) {
+            const float* rp = static_cast<const float*>(ep.residual) + row * ep.ld_res + col0;
+            if (full) {
 #pragma unroll
-            for (int i = 0; i < n / 8; ++i) {
-                uint32_t w[4];
+                for (int i = 0; i < n / 4; ++i) rc.u[i] = ld_nc_v4(rp + 4 * i);
+            } else {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const long long c = col0 + 8 * i + 2 * e;
-                    const uint32_t lo = (c < N) ? __half_as_ushort(rp[8 * i + 2 * e]) : 0u;
-                    const uint32_t hi = (c + 1 < N) ? __half_as_ushort(rp[8 * i + 2 * e + 1]) : 0u;
-                    w[e] = lo | (hi << 16);
+                for (int i = 0; i < n / 4; ++i) {
+                    float x[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) x[e] = (col0 + 4 * i + e < N) ? rp[4 * i + e] : 0.f;
+                    rc.u[i] = make_uint4(__float_as_uint(x[0]), __float_as_uint(x[1]), __float_as_uint(x[2]),
+                                         __float_as_uint(x[3]));
                 }
-                rc.u[i] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        } else {
+            const __half* rp = static_cast<const __half*>(ep.residual) + row * ep.ld_res + col0;
+            if (full) {
+#pragma unroll
+                for (int i = 0; i < n / 8; ++i) rc.u[i] = ld_nc_v4(rp + 8 * i);
+            } else {
+#pragma unroll
+                for (int i = 0; i < n / 8; ++i) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const long long c = col0 + 8 * i + 2 * e;
+                        const uint32_t lo = (c < N) ? __half_as_ushort(rp[8 * i + 2 * e]) : 0u;
+                        const uint32_t hi = (c + 1 < N) ? __half_as_ushort(rp[8 * i + 2 * e + 1]) : 0u;
+                        w[e] = lo | (hi << 16);
+                    }
+                    rc.u[i] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
             }
         }
     }
 }
 
-// Apply the epilogue to n consecutive columns [col0, col0+n) of one row.
-// Columns outside [0, N) get zero bias; the caller never stores them.
-template <int n>
-__device__ __forceinline__ void epi_apply_chunk(float (&v)[n], const ResChunk<n>& rc, long long col0,
-                                                long long N, const EpiParams& ep) {
+// Bias of one output tile, 8 fp16 values per lane: lane l holds columns
+// [tile_col0 + 8l, tile_col0 + 8l + 8).  Loaded once per tile, before the
+// accumulator wait, and broadcast to the chunk loop by warp shuffles.
+__device__ __forceinline__ uint4 bias_tile_load(long long tile_col0, int tile_cols, int lane, long long N,
+                                                const EpiParams& ep) {
+    uint4 b = make_uint4(0u, 0u, 0u, 0u);
+    if (!(ep.flags & EPI_BIAS) || lane * 8 >= tile_cols) return b;
+    const long long c = tile_col0 + lane * 8;
+    if ((ep.flags & EPI_BIAS_VEC) && c + 8 <= N) return __ldg(reinterpret_cast<const uint4*>(ep.bias + c));
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const uint32_t lo = (c + 2 * e < N) ? __half_as_ushort(ep.bias[c + 2 * e]) : 0u;
+        const uint32_t hi = (c + 2 * e + 1 < N) ? __half_as_ushort(ep.bias[c + 2 * e + 1]) : 0u;
+        w[e] = lo | (hi << 16);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Epilogue of one row chunk of n columns starting at tile column `tc` (a
+// multiple of 8), in two phases so the caller can refill `rc` in between:
+//   epi_linear: v = alpha*v (+ bias[j]) (+ R[i][j])
+//   epi_gelu:   v = GeLU(v)                     GELU: 0 none, 1 tanh, 2 erf
+// `bias8` is this lane's bias_tile_load value.
+template <int n, int RES>
+__device__ __forceinline__ void epi_linear(float (&v)[n], const ResChunk<n, RES>& rc, uint4 bias8, int tc,
+                                           const EpiParams& ep) {
     const int flags = ep.flags;
-    if ((flags & (EPI_BIAS | EPI_RES | EPI_SCALE | EPI_GELU_TANH | EPI_GELU_ERF)) == 0) return;
+    if (flags & EPI_SCALE) {
 #pragma unroll
-    for (int g = 0; g < n; g += 8) {
-        float b[8];
-        float r[8];
+        for (int i = 0; i < n; ++i) v[i] *= ep.alpha;
+    }
+    if (flags & EPI_BIAS) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            b[e] = 0.f;
-            r[e] = 0.f;
+        for (int g = 0; g < n; g += 8) {
+            const int src = (tc + g) >> 3;
+            uint4 u;
+            u.x = __shfl_sync(0xffffffffu, bias8.x, src);
+            u.y = __shfl_sync(0xffffffffu, bias8.y, src);
+            u.z = __shfl_sync(0xffffffffu, bias8.z, src);
+            u.w = __shfl_sync(0xffffffffu, bias8.w, src);
+            float b[8];
+            unpack_h8(u, b);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[g + e] += b[e];
         }
-        if (flags & EPI_BIAS) {
-            if ((flags & EPI_BIAS_VEC) && col0 + g + 8 <= N) {
-                unpack_h8(__ldg(reinterpret_cast<const uint4*>(ep.bias + col0 + g)), b);
-            } else {
+    }
+    if constexpr (RES == 2) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    if (col0 + g + e < N) b[e] = __half2float(ep.bias[col0 + g + e]);
-            }
+        for (int i = 0; i < n / 4; ++i) {
+            v[4 * i + 0] += __uint_as_float(rc.u[i].x);
+            v[4 * i + 1] += __uint_as_float(rc.u[i].y);
+            v[4 * i + 2] += __uint_as_float(rc.u[i].z);
+            v[4 * i + 3] += __uint_as_float(rc.u[i].w);
         }
-        if (flags & EPI_RES) {
-            if (flags & EPI_RES_F32) {
-                const uint4 u0 = rc.u[g / 4], u1 = rc.u[g / 4 + 1];
-                r[0] = __uint_as_float(u0.x); r[1] = __uint_as_float(u0.y);
-                r[2] = __uint_as_float(u0.z); r[3] = __uint_as_float(u0.w);
-                r[4] = __uint_as_float(u1.x); r[5] = __uint_as_float(u1.y);
-                r[6] = __uint_as_float(u1.z); r[7] = __uint_as_float(u1.w);
-            } else {
-                unpack_h8(rc.u[g / 8], r);
-            }
-        }
+    } else if constexpr (RES == 1) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[g + e] = epi_scalar(v[g + e], b[e], r[e], flags, ep.alpha);
+        for (int i = 0; i < n / 8; ++i) {
+            float r[8];
+            unpack_h8(rc.u[i], r);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[8 * i + e] += r[e];
+        }
+    }
+}
+
+template <int n, int GELU>
+__device__ __forceinline__ void epi_gelu(float (&v)[n]) {
+    if constexpr (GELU == 1) {
+#pragma unroll
+        for (int i = 0; i < n; ++i) v[i] = gelu_tanh(v[i]);
+    } else if constexpr (GELU == 2) {
+#pragma unroll
+        for (int i = 0; i < n; ++i) v[i] = gelu_erf(v[i]);
     }
 }
 

@@ -1,353 +1,14 @@
-// gemm_tc.cu -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
-//
-//   C[M][N] = epi(A[M][K] . B[K][N]),  A, B fp16 row-major, fp32 accumulate in
-//   TMEM, C fp32 or fp16 row-major.
-//
-// Replaces the reference's sm_86 kernels on the GEMM path
-// (src/rtx_gemm_wmma.cu:23-105, src/rtx_gemm_pipeline.cu:119-325,
-// src/rtx_gemm_epilogue.cu:243-356); the epilogue semantics are those of
-// src/rtx_gemm_epilogue.cu:176-233 (see epilogue.cuh).
-//
-// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: A tile 128x64 (K-major) and B tile 64xBN
-//               (N-major) per k-block into a STAGES-deep ring of
-//               128B-swizzled shared-memory slots, mbarrier full/empty pairs.
-//   warp 1      MMA issuer: allocates TMEM (2 accumulators of 128 lanes x BN
-//               fp32 columns), issues tcgen05.mma M=128 N=BN K=16 (four per
-//               k-block), commits slot releases and accumulator-ready.
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x {32|64} columns, bias /
-//               residual / GeLU in registers, fp32->fp16, swizzled staging
-//               in shared memory, TMA store.  Accumulator i is handed back to
-//               the MMA warp as soon as it is read, so the epilogue of tile t
-//               overlaps the main loop of tile t+1.
-// Ragged M/N/K edges: TMA zero-fills out-of-range loads and clips stores.
+// gemm_tc.cu -- tile-shape choice and dispatch for the tcgen05 GEMM
+// (kernel in gemm_tc.cuh, instantiated in gemm_tc_f16.cu / gemm_tc_f32.cu).
 #include "internal.h"
-#include "sm100.cuh"
-#include "epilogue.cuh"
-
-#include <cudaTypedefs.h>
-#include <mutex>
-#include <stdio.h>
+#include "gemm_tc.cuh"
 
 namespace pax {
 
-struct TcParams {
-    int M, N, K;
-    int tiles_m, tiles_n, num_tiles;
-    int group_m;  // output tiles are visited in column-major groups of group_m tile rows
-    EpiParams epi;
-};
-
-template <int BN_, int STAGES_, typename OutT>
-struct TcCfg {
-    static constexpr int BM = 128, BN = BN_, BK = 64, STAGES = STAGES_;
-    static constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KiB
-    static constexpr uint32_t B_BYTES = BN * BK * 2;  // 16 / 32 KiB
-    static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int EPI_COLS = 128 / (int)sizeof(OutT);  // one 128-byte row per chunk
-    static constexpr uint32_t STG_BYTES = 32 * 128;            // per warp, per buffer
-    static constexpr uint32_t STG_TOTAL = 4 * 2 * STG_BYTES;
-    static constexpr uint32_t TMEM_COLS = 2 * BN;
-    static constexpr uint32_t NUM_BARS = 2 * STAGES + 5;
-    static constexpr size_t SMEM_BYTES =
-        1024 + (size_t)STAGES * STAGE_BYTES + STG_TOTAL + NUM_BARS * 8 + 16;
-    static constexpr uint32_t IDESC = umma_idesc_f16(BM, BN, /*a_mn*/ false, /*b_mn*/ true);
-    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-    static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
-};
-
-__device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& mb, int& nb) {
-    const int per_group = p.group_m * p.tiles_n;
-    const int g = t / per_group;
-    const int first_m = g * p.group_m;
-    const int gm = min(p.tiles_m - first_m, p.group_m);
-    const int r = t - g * per_group;
-    mb = first_m + r % gm;
-    nb = r / gm;
-}
-
-template <int BN, int STAGES, typename OutT>
-__global__ void __launch_bounds__(192, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, const TcParams p) {
-    using Cfg = TcCfg<BN, STAGES, OutT>;
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem =
-        reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;
-    uint8_t* sB = sA + STAGES * Cfg::A_BYTES;
-    uint8_t* sStg = sB + STAGES * Cfg::B_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sStg + Cfg::STG_TOTAL);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NUM_BARS);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-    const uint32_t bar0 = smem_u32(bars);
-    const uint32_t full0 = bar0;                     // [STAGES]
-    const uint32_t empty0 = bar0 + 8u * STAGES;      // [STAGES]
-    const uint32_t tfull0 = bar0 + 16u * STAGES;     // [2]
-    const uint32_t tempty0 = tfull0 + 16u;           // [2]
-    const uint32_t drain_bar = tempty0 + 16u;
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(full0 + 8u * s, 1);
-            mbar_init(empty0 + 8u * s, 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(tfull0 + 8u * b, 1);
-            mbar_init(tempty0 + 8u * b, 4);  // one arrive per epilogue warp
-        }
-        mbar_init(drain_bar, 1);
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    if (warp == 0 && lane == 0) {
-        tma_prefetch_desc(&tmA);
-        tma_prefetch_desc(&tmB);
-        tma_prefetch_desc(&tmC);
-    }
-    if (warp == 1) {
-        tmem_alloc<1>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
-        tmem_relinquish<1>();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-    const int num_kb = (p.K + Cfg::BK - 1) / Cfg::BK;
-
-    if (warp == 0) {
-        // ------------------------------------------------ TMA producer
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            uint32_t issued = 0, last_parity = 0;
-            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-                int mb, nb;
-                tile_coords(t, p, mb, nb);
-                for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t fb = full0 + 8u * stage;
-                    mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
-                    tma_load_2d(smem_u32(sA + stage * Cfg::A_BYTES), &tmA, fb, kb * Cfg::BK, mb * Cfg::BM);
-#pragma unroll
-                    for (int j = 0; j < BN / 64; ++j)
-                        tma_load_2d(smem_u32(sB + stage * Cfg::B_BYTES + j * 8192), &tmB, fb,
-                                    nb * BN + j * 64, kb * Cfg::BK);
-                    issued |= 1u << stage;
-                    last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-            }
-            if (!ok) {
-                // Abort: every TMA load issued must land before the CTA exits.
-                for (int s = 0; s < STAGES; ++s)
-                    if (issued & (1u << s)) mbar_wait(full0 + 8u * s, (last_parity >> s) & 1u, nullptr);
-            }
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            int acc = 0;
-            uint32_t acc_phase = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-                if (!mbar_wait(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-                for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(full0 + 8u * stage, phase, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + stage * Cfg::A_BYTES);
-                    const uint32_t b0 = smem_u32(sB + stage * Cfg::B_BYTES);
-#pragma unroll
-                    for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
-                        const uint64_t ad = umma_desc_sw128(a0 + kk * 32, 16, 1024);
-                        const uint64_t bd = umma_desc_sw128(b0 + kk * 2048, 8192, 1024);
-                        tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (kb | kk) != 0 ? 1u : 0u);
-                    }
-                    tc_commit(empty0 + 8u * stage);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-                if (!ok) break;
-                tc_commit(tfull0 + 8u * acc);
-                if (++acc == 2) {
-                    acc = 0;
-                    acc_phase ^= 1u;
-                }
-            }
-            // No MMA may still be writing TMEM when it is released.
-            tc_commit(drain_bar);
-            mbar_wait(drain_bar, 0, nullptr);
-        }
-    } else {
-        // ------------------------------------------------ epilogue warps
-        constexpr int EC = Cfg::EPI_COLS;
-        const int q = warp & 3;  // TMEM lane quarter this warp may read
-        uint8_t* stg = sStg + (warp - 2) * 2 * Cfg::STG_BYTES;
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        int sb = 0;
-        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-            int mb, nb;
-            tile_coords(t, p, mb, nb);
-            bool ok = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag);
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            tc_fence_after();
-            const long long row = (long long)mb * Cfg::BM + q * 32 + lane;
-            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-            for (int c = 0; c < BN; c += EC) {
-                const long long col0 = (long long)nb * BN + c;
-                ResChunk<EC> rc;
-                res_prefetch<EC>(rc, row, col0, p.M, p.N, p.epi);
-                float v[EC];
-                tmem_ld_32x32b_x32(t_row + (uint32_t)c, v);
-                if constexpr (EC == 64) tmem_ld_32x32b_x32(t_row + (uint32_t)c + 32u, v + 32);
-                tmem_wait_ld();
-                if (c + EC >= BN) {
-                    // Whole accumulator read: hand it back to the MMA warp.
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(tempty0 + 8u * acc);
-                }
-                epi_apply_chunk<EC>(v, rc, col0, p.N, p.epi);
-                // Staging buffer sb is free once at most one store group (the
-                // one using the other buffer) is still reading shared memory.
-                if (lane == 0) bulk_wait_read<1>();
-                __syncwarp();
-                const uint32_t srow = smem_u32(stg + sb * Cfg::STG_BYTES) + (uint32_t)lane * 128u;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    uint32_t w0, w1, w2, w3;
-                    if constexpr (sizeof(OutT) == 2) {
-                        w0 = pack_half2(v[8 * j + 0], v[8 * j + 1]);
-                        w1 = pack_half2(v[8 * j + 2], v[8 * j + 3]);
-                        w2 = pack_half2(v[8 * j + 4], v[8 * j + 5]);
-                        w3 = pack_half2(v[8 * j + 6], v[8 * j + 7]);
-                    } else {
-                        w0 = __float_as_uint(v[4 * j + 0]);
-                        w1 = __float_as_uint(v[4 * j + 1]);
-                        w2 = __float_as_uint(v[4 * j + 2]);
-                        w3 = __float_as_uint(v[4 * j + 3]);
-                    }
-                    // 128B swizzle: 16-byte chunk j of row r lives at chunk j ^ (r % 8).
-                    st_shared_v4(srow + (uint32_t)((j ^ (lane & 7)) << 4), w0, w1, w2, w3);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                const int row0 = mb * Cfg::BM + q * 32;
-                if (lane == 0 && col0 < p.N && row0 < p.M) {  // boxes wholly outside C are skipped
-                    tma_store_2d(&tmC, smem_u32(stg + sb * Cfg::STG_BYTES), (int)col0, row0);
-                    bulk_commit();
-                }
-                sb ^= 1;
-            }
-            if (++acc == 2) {
-                acc = 0;
-                acc_phase ^= 1u;
-            }
-        }
-        if (lane == 0) bulk_wait<0>();
-        __syncwarp();
-    }
-
-    __syncwarp();
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc<1>(tmem_base, Cfg::TMEM_COLS);
-    }
-}
-
-// ======================================================================
-// Host side
-// ======================================================================
-
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// 2-D row-major tensor map: `inner` contiguous elements per row, `outer`
-// rows `pitch` bytes apart, box of box_inner x box_outer, 128B swizzle.
-static bool make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
-                      uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
-    auto enc = tensor_map_encoder();
-    if (!enc) return false;
-    cuuint64_t dims[2] = {inner, outer};
-    cuuint64_t strides[1] = {pitch_bytes};
-    cuuint32_t box[2] = {box_inner, box_outer};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
-}
-
-template <int BN, int STAGES, typename OutT>
-static pax_status_t launch_tc_impl(const Problem& pr, cudaStream_t stream) {
-    using Cfg = TcCfg<BN, STAGES, OutT>;
-    const bool f16 = sizeof(OutT) == 2;
-    CUtensorMap tA, tB, tC;
-    if (!make_tmap(&tA, pr.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pr.K, pr.M, pr.lda * 2, 64, 128)) return PAX_ERR_CUDA;
-    if (!make_tmap(&tB, pr.B, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pr.N, pr.K, pr.ldb * 2, 64, 64)) return PAX_ERR_CUDA;
-    if (!make_tmap(&tC, pr.C, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pr.N, pr.M,
-                   pr.ldc * (f16 ? 2 : 4), Cfg::EPI_COLS, 32))
-        return PAX_ERR_CUDA;
-
-    TcParams p;
-    p.M = (int)pr.M;
-    p.N = (int)pr.N;
-    p.K = (int)pr.K;
-    p.tiles_m = (int)((pr.M + Cfg::BM - 1) / Cfg::BM);
-    p.tiles_n = (int)((pr.N + BN - 1) / BN);
-    p.num_tiles = p.tiles_m * p.tiles_n;
-    p.group_m = 8;
-    p.epi = pr.epi;
-
-    const int dev = current_device();
-    const int sms = device_sm_count(dev);
-    auto kern = gemm_tc_kernel<BN, STAGES, OutT>;
-    // Attribute is per device; setting it again is cheap and idempotent.
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES) != cudaSuccess)
-        return PAX_ERR_CUDA;
-    const int grid = p.num_tiles < sms ? p.num_tiles : sms;
-    kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(tA, tB, tC, p);
-    return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
-}
-
-constexpr int kStages256 = 4;
-constexpr int kStages128 = 6;
+pax_status_t launch_tc_f16(const Problem& p, int bn, cudaStream_t stream);
+pax_status_t launch_tc_f32(const Problem& p, int bn, cudaStream_t stream);
+int read_clear_device_error_tc_f16();
+int read_clear_device_error_tc_f32();
 
 size_t tc_smem_bytes(int bn, bool c_f16) {
     if (bn == 256)
@@ -367,19 +28,14 @@ int tc_pick_bn(long long M, long long N, int sms) {
 
 pax_status_t launch_tc(const Problem& p, int bn, cudaStream_t stream) {
     if (p.M > 0x7fffffffLL || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
-    if (bn == 256) {
-        return p.c_f16 ? launch_tc_impl<256, kStages256, __half>(p, stream)
-                       : launch_tc_impl<256, kStages256, float>(p, stream);
-    }
-    return p.c_f16 ? launch_tc_impl<128, kStages128, __half>(p, stream)
-                   : launch_tc_impl<128, kStages128, float>(p, stream);
+    return p.c_f16 ? launch_tc_f16(p, bn == 256 ? 256 : 128, stream) : launch_tc_f32(p, bn == 256 ? 256 : 128, stream);
 }
 
 int read_clear_device_error_tc() {
-    int v = 0, z = 0;
-    if (cudaMemcpyFromSymbol(&v, g_pax_device_error, sizeof(int)) != cudaSuccess) return -1;
-    if (v) cudaMemcpyToSymbol(g_pax_device_error, &z, sizeof(int));
-    return v;
+    const int a = read_clear_device_error_tc_f16();
+    const int b = read_clear_device_error_tc_f32();
+    if (a < 0 || b < 0) return -1;
+    return a | b;
 }
 
 }  // namespace pax

@@ -1,0 +1,12 @@
+// gemm_tc_f16.cu -- instantiates the tcgen05 GEMM (gemm_tc.cuh) for fp16 C.
+#include "gemm_tc.cuh"
+
+namespace pax {
+
+pax_status_t launch_tc_f16(const Problem& p, int bn, cudaStream_t stream) {
+    return launch_tc_typed<__half>(p, bn, stream);
+}
+
+int read_clear_device_error_tc_f16() { return read_clear_device_error_this_unit(); }
+
+}  // namespace pax

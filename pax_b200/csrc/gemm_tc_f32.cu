@@ -1,0 +1,12 @@
+// gemm_tc_f32.cu -- instantiates the tcgen05 GEMM (gemm_tc.cuh) for fp32 C.
+#include "gemm_tc.cuh"
+
+namespace pax {
+
+pax_status_t launch_tc_f32(const Problem& p, int bn, cudaStream_t stream) {
+    return launch_tc_typed<float>(p, bn, stream);
+}
+
+int read_clear_device_error_tc_f32() { return read_clear_device_error_this_unit(); }
+
+}  // namespace pax

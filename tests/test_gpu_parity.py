@@ -26,6 +26,19 @@ def stream_ptr():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
+class _DevArray:
+    """Exposes a raw device pointer to torch via __cuda_array_interface__."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (int(ptr), False), "shape": tuple(shape), "typestr": typestr,
+                                         "version": 3, "strides": None}
+
+
+def dev_view(ptr, shape, dtype) -> torch.Tensor:
+    typestr = {np.float16: "<f2", np.float32: "<f4"}[dtype]
+    return torch.as_tensor(_DevArray(ptr, shape, typestr), device="cuda")
+
+
 # ---------------------------------------------------------------- tcgen05 core
 @pytest.mark.parametrize("bn", [256, 128])
 @pytest.mark.parametrize("shape", [(128, 256, 64), (256, 512, 128), (384, 768, 1024)])
@@ -225,16 +238,24 @@ def test_dispatchers_with_library_buffers(cuda, rng):
     try:
         assert bA.base and bB.base and bC.base and bBias.base
         for buf, arr in ((bA, A), (bB, B), (bBias, bias)):
-            torch.cuda.cudart().cudaMemcpy(buf.base, arr.ctypes.data, arr.nbytes, 1)
+            dev_view(buf.base, arr.shape, np.float16).copy_(torch.from_numpy(arr))
         L.pax_dispatch_bias_gelu(ctypes.byref(bA), ctypes.byref(bB), ctypes.byref(bC), bBias.base, s)
         torch.cuda.synchronize()
-        out = np.empty((M, N), np.float32)
-        torch.cuda.cudart().cudaMemcpy(out.ctypes.data, bC.base, out.nbytes, 2)
+        out = dev_view(bC.base, (M, N), np.float32).cpu().numpy()
         check(out, oracle.gemm(A, B, "bias_gelu_tanh", bias=bias), np.float32)
         L.pax_dispatch_pipeline_gemm(ctypes.byref(bA), ctypes.byref(bB), ctypes.byref(bC), s)
         torch.cuda.synchronize()
-        torch.cuda.cudart().cudaMemcpy(out.ctypes.data, bC.base, out.nbytes, 2)
+        out = dev_view(bC.base, (M, N), np.float32).cpu().numpy()
         check(out, oracle.gemm(A, B), np.float32)
+        # fp16 C through the same dispatcher: elem_size 2 selects fp16 output
+        bC16 = L.pax_alloc_device_2d(M, N, 2, s)
+        try:
+            L.pax_dispatch_wmma_gemm(ctypes.byref(bA), ctypes.byref(bB), ctypes.byref(bC16), s)
+            torch.cuda.synchronize()
+            out16 = dev_view(bC16.base, (M, N), np.float16).cpu().numpy()
+            check(out16, oracle.gemm(A, B, out_dtype=np.float16), np.float16)
+        finally:
+            L.pax_free_device(ctypes.byref(bC16))
     finally:
         for b in (bA, bB, bC, bBias):
             L.pax_free_device(ctypes.byref(b))
