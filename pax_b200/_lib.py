@@ -1,6 +1,6 @@
-"""Loads ``libpax_b200.so`` (the C ABI of include/pax.h) and declares its
-signatures.  There is no fallback: if the library is missing, importing the
-package fails with instructions to build it."""
+"""Loads ``libpax_b200.so`` (the C ABI of include/pax.h) on first use and
+declares its signatures.  There is no fallback: if the library is missing,
+the first call raises LibraryNotBuilt with instructions to build it."""
 from __future__ import annotations
 
 import ctypes
@@ -113,6 +113,23 @@ def _declare(L: ctypes.CDLL) -> None:
         fn.restype = res
 
 
+_LIB: ctypes.CDLL | None = None
+
+
+def get() -> ctypes.CDLL:
+    """The loaded library; raises LibraryNotBuilt if it has not been built."""
+    global _LIB
+    if _LIB is None:
+        _LIB = load()
+    return _LIB
+
+
+def __getattr__(name):
+    if name == "lib":
+        return get()
+    raise AttributeError(name)
+
+
 def load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise LibraryNotBuilt(
@@ -126,5 +143,3 @@ def load() -> ctypes.CDLL:
         raise ImportError("pax_gemm_desc_t layout mismatch between libpax_b200.so and the Python binding")
     return L
 
-
-lib = load()

@@ -8,7 +8,8 @@ from enum import IntEnum
 
 import torch
 
-from ._lib import GemmDesc, lib
+from . import _lib
+from ._lib import GemmDesc
 
 
 class Status(IntEnum):
@@ -49,7 +50,7 @@ class Algo(IntEnum):
 class PaxError(RuntimeError):
     def __init__(self, status: int, what: str = ""):
         self.status = Status(status)
-        msg = lib.pax_status_string(int(status)).decode()
+        msg = _lib.get().pax_status_string(int(status)).decode()
         super().__init__(f"{what}: {msg} ({self.status.name})" if what else msg)
 
 
@@ -111,7 +112,7 @@ def gemm(A: torch.Tensor, B: torch.Tensor, *, epilogue="none", bias=None, residu
         out = torch.empty((A.shape[0], B.shape[1]), dtype=out_dtype, device=A.device)
     d = make_desc(A, B, out, epilogue, bias, residual, alpha, algo)
     s = stream if stream is not None else torch.cuda.current_stream(A.device)
-    st = lib.pax_gemm_ex(ctypes.byref(d), ctypes.c_void_p(s.cuda_stream))
+    st = _lib.get().pax_gemm_ex(ctypes.byref(d), ctypes.c_void_p(s.cuda_stream))
     if st != 0:
         raise PaxError(st, "pax_gemm_ex")
     return out
@@ -120,13 +121,13 @@ def gemm(A: torch.Tensor, B: torch.Tensor, *, epilogue="none", bias=None, residu
 def select_algo(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, **kw) -> Algo:
     """The algorithm pax_gemm_ex would run (host-only)."""
     d = make_desc(A, B, C, **kw)
-    return Algo(lib.pax_gemm_select_algo(ctypes.byref(d)))
+    return Algo(_lib.get().pax_gemm_select_algo(ctypes.byref(d)))
 
 
 def device_error() -> Status:
     """Read and clear the device error word (synchronises the device)."""
-    return Status(lib.pax_device_error())
+    return Status(_lib.get().pax_device_error())
 
 
 def last_error() -> Status:
-    return Status(lib.pax_last_error())
+    return Status(_lib.get().pax_last_error())
