@@ -81,34 +81,43 @@ bool tma_compatible(const Problem& p) {
 }
 
 // --------------------------------------------------------- workspaces
-// Split-K partial sums of the skinny kernel, one buffer per (device, stream)
-// so that launches on different streams never share one.  Layout:
-// [counters, padded to 256 B][partial sums].
+// Split-K scratch of the skinny kernel, one buffer per (device, stream) so
+// that launches on different streams never share one.  Layout:
+// [per-tile counters: cnt_cap bytes][partial sums: ws_cap bytes].  The
+// counters must be zero when a launch starts; the kernel returns every
+// counter it used to zero, and the counter region never moves or shrinks
+// while the buffer lives, so zero counters stay zero across calls of any
+// shape.  Growing either region reallocates and zeroes the whole buffer.
 struct Workspace {
     void* ptr = nullptr;
-    size_t bytes = 0;
+    size_t cnt_cap = 0;
+    size_t ws_cap = 0;
 };
 static std::mutex g_ws_mu;
 static std::map<std::pair<int, uintptr_t>, Workspace> g_ws;
 
-static pax_status_t get_workspace(int dev, cudaStream_t s, size_t need, void** out) {
+static pax_status_t get_workspace(int dev, cudaStream_t s, size_t cnt_need, size_t ws_need, int** counters,
+                                  float** partials) {
     std::lock_guard<std::mutex> lk(g_ws_mu);
     Workspace& w = g_ws[{dev, reinterpret_cast<uintptr_t>(s)}];
-    if (w.bytes < need) {
+    if (w.cnt_cap < cnt_need || w.ws_cap < ws_need) {
+        const size_t cnt_cap = w.cnt_cap > cnt_need ? w.cnt_cap : cnt_need;
+        const size_t ws_cap = w.ws_cap > ws_need ? w.ws_cap : ws_need;
         if (w.ptr) {
             cudaStreamSynchronize(s);
             cudaFree(w.ptr);
-            w.ptr = nullptr;
-            w.bytes = 0;
+            w = Workspace();
         }
-        if (cudaMalloc(&w.ptr, need) != cudaSuccess) {
-            w.ptr = nullptr;
+        if (cudaMalloc(&w.ptr, cnt_cap + ws_cap) != cudaSuccess) {
+            w = Workspace();
             return PAX_ERR_ALLOC;
         }
-        if (cudaMemsetAsync(w.ptr, 0, need, s) != cudaSuccess) return PAX_ERR_CUDA;
-        w.bytes = need;
+        if (cudaMemsetAsync(w.ptr, 0, cnt_cap + ws_cap, s) != cudaSuccess) return PAX_ERR_CUDA;
+        w.cnt_cap = cnt_cap;
+        w.ws_cap = ws_cap;
     }
-    *out = w.ptr;
+    *counters = static_cast<int*>(w.ptr);
+    *partials = reinterpret_cast<float*>(static_cast<char*>(w.ptr) + w.cnt_cap);
     return PAX_OK;
 }
 
@@ -222,11 +231,11 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
             size_t ws_bytes, cnt_bytes;
             skinny_geometry(p.M, p.N, p.K, di.sms, &grid, &ws_bytes, &cnt_bytes);
             const size_t cnt_pad = (cnt_bytes + 255) & ~size_t(255);
-            void* ws = nullptr;
-            st = get_workspace(dev, s, cnt_pad + ws_bytes, &ws);
+            int* counters = nullptr;
+            float* partials = nullptr;
+            st = get_workspace(dev, s, cnt_pad, ws_bytes, &counters, &partials);
             if (st != PAX_OK) return fail(st, "skinny workspace allocation failed (%zu bytes)", cnt_pad + ws_bytes);
-            st = launch_skinny_ws(p, grid, reinterpret_cast<float*>(static_cast<char*>(ws) + cnt_pad),
-                                  static_cast<int*>(ws), s);
+            st = launch_skinny_ws(p, grid, partials, counters, s);
             break;
         }
         case PAX_ALGO_SIMT: st = launch_simt(p, s); break;

@@ -111,6 +111,15 @@ def test_skinny_epilogues(cuda, rng, epi, out):
     check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
 
 
+def test_skinny_workspace_reuse_across_shapes(cuda, rng):
+    """The per-stream workspace is reused by later calls with more column
+    tiles (more counters) and larger partial-sum needs, and fewer again."""
+    for M, N, K in [(16, 256, 4096), (16, 16384, 4096), (48, 2048, 1024), (16, 16384, 4096), (1, 128, 64)]:
+        A, B = inputs(rng, M, N, K, dist="normal")
+        got = run_gemm(A, B, cuda, out_dtype=np.float16, algo="skinny")
+        check(got, oracle.gemm(A, B, out_dtype=np.float16), np.float16)
+
+
 # ---------------------------------------------------------------- SIMT
 @pytest.mark.parametrize("shape", [(1, 1, 1), (17, 17, 17), (127, 33, 129), (5, 300, 7), (64, 64, 0)])
 @pytest.mark.parametrize("epi", ["none", "bias_gelu_tanh", "residual_gelu_erf"])
