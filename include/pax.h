@@ -190,6 +190,23 @@ void pax_gemm_residual_gelu_erf_f16_launch(const __half* A, const __half* B, __h
 /* General entry point with status return (new). */
 pax_status_t pax_gemm_ex(const pax_gemm_desc_t* desc, cudaStream_t stream);
 
+/* Skinny GEMM (1 <= M <= 64) without any allocation.  No counterpart in the
+ * reference.
+ * For callers that cannot let a library allocate device memory: processes
+ * whose GPU memory is owned by their own allocator (a framework's caching
+ * allocator, a serving process that reserves memory at start-up) and loops
+ * that cannot afford the device synchronisation of cudaMalloc/cudaFree.
+ * Same arithmetic as pax_gemm_ex with PAX_ALGO_SKINNY (desc->algo is
+ * ignored), but the split-K scratch is a fixed 8 MiB array inside the
+ * library, held by every GPU that loads it until the process exits.  Calls
+ * no cudaMalloc/cudaFree.  Problems whose scratch need exceeds 8 MiB
+ * (roughly m > 48 at 148 SMs) return PAX_ERR_UNSUPPORTED with a message.
+ * The first call on a device looks up the array's device address, so make
+ * it before any stream capture.  All calls share the array: calls that
+ * overlap on the GPU (different streams, or devices sharing nothing but the
+ * process) on the same device race and give wrong results. */
+pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cudaStream_t stream);
+
 /* The algorithm pax_gemm_ex would run for desc with algo = PAX_ALGO_AUTO (new;
  * host-only, launches nothing). */
 pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc);

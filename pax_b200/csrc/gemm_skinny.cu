@@ -22,6 +22,7 @@
 
 #include <cudaTypedefs.h>
 #include <mutex>
+#include <stdio.h>
 
 namespace pax {
 
@@ -392,4 +393,77 @@ int read_clear_device_error_skinny() {
     return v;
 }
 
+// ----------------------------------------------------------------------
+// Allocation-free variant (pax_gemm_skinny_noalloc).
+//
+// Some callers cannot let a library call cudaMalloc: processes whose device
+// memory is owned by their own allocator (a framework's caching allocator,
+// or a serving process that reserves the GPU's memory at start-up and treats
+// any later allocation as a failure), and latency-critical loops where the
+// implicit device synchronisation of cudaMalloc/cudaFree is not acceptable.
+// For them the skinny kernel's scratch (per-tile arrival counters followed
+// by the fp32 partial sums) lives in this fixed array instead of the
+// per-stream workspace.  Every GPU that loads the library holds it until the
+// process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_skinny_scratch[kNoAllocScratchBytes];
+
+// Device address of g_skinny_scratch, looked up once per device (the host
+// symbol is only a handle; passing it to a kernel would be wrong).
+constexpr int kNoAllocMaxDevices = 64;
+static std::mutex g_scratch_mu;
+static void* g_scratch_addr[kNoAllocMaxDevices];
+
+static pax_status_t scratch_address(int dev, void** out) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_skinny_scratch) != cudaSuccess || ptr == nullptr) return PAX_ERR_CUDA;
+        g_scratch_addr[dev] = ptr;
+    }
+    *out = g_scratch_addr[dev];
+    return PAX_OK;
+}
+
 }  // namespace pax
+
+extern "C" pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cudaStream_t stream) {
+    using namespace pax;
+    Problem p;
+    pax_status_t st = normalize_desc(desc, &p);
+    if (st != PAX_OK) return st;
+    if (p.M == 0 || p.N == 0) return report_status(PAX_OK, "");
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return report_status(PAX_ERR_CUDA, "pax_gemm_skinny_noalloc: no device");
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return report_status(PAX_ERR_UNSUPPORTED, "pax_gemm_skinny_noalloc: device index above 63");
+    int major = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (major != 10) return report_status(PAX_ERR_NO_DEVICE, "pax_gemm_skinny_noalloc: needs an sm_100 device");
+    if (p.M > kSkinnyMaxM || !tma_compatible(p))
+        return report_status(PAX_ERR_UNSUPPORTED,
+                             "pax_gemm_skinny_noalloc: needs 1 <= m <= 64, k >= 1 and 16-byte aligned rows");
+    int grid;
+    size_t ws_bytes, cnt_bytes;
+    skinny_geometry(p.M, p.N, p.K, sms, &grid, &ws_bytes, &cnt_bytes);
+    const size_t cnt_pad = (cnt_bytes + 255) & ~size_t(255);
+    if (cnt_pad + ws_bytes > kNoAllocScratchBytes) {
+        char msg[160];
+        snprintf(msg, sizeof msg,
+                 "pax_gemm_skinny_noalloc: problem needs %zu bytes of scratch, above the fixed %zu-byte limit",
+                 cnt_pad + ws_bytes, kNoAllocScratchBytes);
+        return report_status(PAX_ERR_UNSUPPORTED, msg);
+    }
+    void* scratch = nullptr;
+    if (scratch_address(dev, &scratch) != PAX_OK)
+        return report_status(PAX_ERR_CUDA, "pax_gemm_skinny_noalloc: cudaGetSymbolAddress failed");
+    // The array keeps whatever the previous call left; the counters must
+    // start at zero.
+    if (cudaMemsetAsync(scratch, 0, cnt_pad, stream) != cudaSuccess)
+        return report_status(PAX_ERR_CUDA, "pax_gemm_skinny_noalloc: counter reset failed");
+    st = launch_skinny_ws(p, grid, reinterpret_cast<float*>(static_cast<char*>(scratch) + cnt_pad),
+                          static_cast<int*>(scratch), stream);
+    if (st != PAX_OK) return report_status(st, "pax_gemm_skinny_noalloc: launch failed");
+    return report_status(PAX_OK, "");
+}

@@ -195,6 +195,13 @@ static pax_status_t normalize(const pax_gemm_desc_t* d, Problem* p) {
     return PAX_OK;
 }
 
+// Internal entry points for other translation units (internal.h).
+pax_status_t normalize_desc(const pax_gemm_desc_t* d, Problem* p) { return normalize(d, p); }
+pax_status_t report_status(pax_status_t s, const char* msg) {
+    if (s == PAX_OK) return set_status(s);
+    return fail(s, "%s", msg);
+}
+
 static pax_algo_t select_algo(const Problem& p) {
     if (!tma_compatible(p)) return PAX_ALGO_SIMT;
     if (p.M <= kSkinnyMaxM) return PAX_ALGO_SKINNY;

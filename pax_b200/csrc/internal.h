@@ -46,6 +46,12 @@ int tc_pick_bn(long long M, long long N, int sms);
 // Largest M the skinny kernel accepts.
 constexpr long long kSkinnyMaxM = 64;
 
+// Descriptor validation and status recording shared with the C-ABI layer
+// (host_bridge.cpp): normalize_desc checks and normalises a descriptor,
+// report_status records a status for pax_last_error() and prints msg.
+pax_status_t normalize_desc(const pax_gemm_desc_t* d, Problem* p);
+pax_status_t report_status(pax_status_t s, const char* msg);
+
 // Read and clear the device error word of each kernel translation unit on
 // the current device.
 int read_clear_device_error_tc();
