@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="pax", choices=["pax", "reference"])
     ap.add_argument("--gather", action="store_true")
+    ap.add_argument("--strong", action="store_true",
+                    help="split the configuration's N over the ranks (fixed total work) instead of N per rank")
     ap.add_argument("--seed", type=int, default=0x5EED)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -160,11 +162,12 @@ def run_reference(args):
 
 
 def workload_config(cfg, world, args):
+    n_total = cfg["N"] if getattr(args, "strong", False) else cfg["N"] * world
     return {
         "workload": cfg["name"],
         "M": cfg["M"],
-        "N_per_gpu": cfg["N"],
-        "N_total": cfg["N"] * world,
+        "N_per_gpu": n_total // world,
+        "N_total": n_total,
         "K": cfg["K"],
         "epilogue": cfg["epi"],
         "inputs": cfg["dist"],
@@ -272,21 +275,32 @@ def run_pax(args):
     if args.epilogue:
         cfg["epi"] = args.epilogue
         cfg["name"] += f" [epilogue overridden: {args.epilogue}]"
-    M, N, K = cfg["M"], cfg["N"], cfg["K"]
+    from pax_b200.dist import equal_slabs, gather_columns, slab_bounds
+
+    M, K = cfg["M"], cfg["K"]
+    if args.strong:
+        n_total = cfg["N"]
+        s0, s1 = slab_bounds(n_total, world, rank)
+        N = s1 - s0
+    else:
+        N = cfg["N"]
+        n_total = N * world
+    if args.gather and not (equal_slabs(n_total, world) or world == 1):
+        raise SystemExit("--gather needs equal slabs (N divisible by 8 * ranks)")
+    ga = torch.Generator(device=dev)
+    ga.manual_seed(args.seed)  # A is replicated: same on every rank
     g = torch.Generator(device=dev)
-    g.manual_seed(args.seed + 1000 * rank)
+    g.manual_seed(args.seed + 1000 * (rank + 1))  # this rank's column slab of B, bias
     if cfg["dist"] == "uniform":
-        A = (torch.rand((M, K), generator=g, device=dev) * 2 - 1).half()
+        A = (torch.rand((M, K), generator=ga, device=dev) * 2 - 1).half()
         B = (torch.rand((K, N), generator=g, device=dev) * 2 - 1).half()
     else:
-        A = torch.randn((M, K), generator=g, device=dev).half()
+        A = torch.randn((M, K), generator=ga, device=dev).half()
         B = (torch.randn((K, N), generator=g, device=dev) * 0.02).half()
     bias = torch.randn((N,), generator=g, device=dev).half()
     res = torch.randn((M, N), generator=g, device=dev).half() if "residual" in cfg["epi"] else None
     C = torch.empty((M, N), dtype=torch.float16, device=dev)
-    gathered = None
-    if args.gather and world > 1:
-        gathered = torch.empty((world, M, N), dtype=torch.float16, device=dev)
+    gathered = args.gather and world > 1
     # L2 flush between steps: write a buffer larger than L2, then read a second
     # one so the dirty lines are written back before the timed launch rather
     # than during it.
@@ -304,8 +318,8 @@ def run_pax(args):
 
     def step():
         pax_b200.gemm(A, B, **kw)
-        if gathered is not None:
-            dist.all_gather_into_tensor(gathered, C)
+        if gathered:
+            gather_columns(C)
 
     for _ in range(args.warmup):
         flush.zero_()
@@ -345,7 +359,8 @@ def run_pax(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     flops_rank = 2.0 * M * N * K
-    value = flops_rank * world / (ms_max * 1e-3) / 1e12
+    flops_total = 2.0 * M * n_total * K
+    value = flops_total / (ms_max * 1e-3) / 1e12
 
     # ---- end to end through the public API: pinned host inputs, host output
     hA = A.cpu().pin_memory()
@@ -387,11 +402,11 @@ def run_pax(args):
     t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = flops_rank * world / (float(t.item()) * 1e-3) / 1e12
+    e2e_value = flops_total / (float(t.item()) * 1e-3) / 1e12
 
     peak, hbm, peak_kind = peaks()
-    kernel_ms = min(ms) if gathered is None else None
-    achieved = flops_rank / (statistics.mean(ms) * 1e-3) / 1e12 if gathered is None else None
+    kernel_ms = None if gathered else min(ms)
+    achieved = None if gathered else flops_rank / (statistics.mean(ms) * 1e-3) / 1e12
     roofline = None
     if achieved is not None:
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -422,13 +437,14 @@ def run_pax(args):
             "warmup": args.warmup,
             "ms_per_step": ms_max,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if args.strong else "weak",
             "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic (seeded torch RNG on device: " + (
                 "A,B uniform[-1,1]" if cfg["dist"] == "uniform" else "A N(0,1), B N(0,0.02)") + ", bias N(0,1))",
             "config": workload_config(cfg, world, args),
             "pct_of_dense_fp16_peak": 100.0 * (value / world) / peak,
+            "gemm_ms_per_rank": ms_max,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},

@@ -1,0 +1,93 @@
+"""Column-slab partitioning and the C all-gather, on CPU ranks (gloo,
+world_size 2 and 4).  The per-slab GEMM is the oracle here; on GPUs it is the
+library kernel (bench.py --gpus N)."""
+from __future__ import annotations
+
+import os
+import queue
+import socket
+import time
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from pax_b200.dist import equal_slabs, gather_columns, local_slab_gemm, slab_bounds
+
+
+def test_slab_bounds_cover_all_columns():
+    for n, w in [(32768, 8), (4096, 2), (1000, 4), (16, 4), (8200, 3)]:
+        spans = [slab_bounds(n, w, r) for r in range(w)]
+        assert spans[0][0] == 0 and spans[-1][1] == n
+        for (a, b), (c, d) in zip(spans, spans[1:]):
+            assert b == c and a <= b
+        for a, b in spans[:-1]:
+            assert a % 8 == 0 and b % 8 == 0
+    assert equal_slabs(32768, 8) and not equal_slabs(1000, 3)
+
+
+def _oracle_gemm(A, B, epilogue="none", bias=None, residual=None, out_dtype=torch.float16):
+    a = A.numpy()
+    b = np.ascontiguousarray(B.numpy())
+    bi = None if bias is None else bias.numpy()
+    r = None if residual is None else np.ascontiguousarray(residual.numpy())
+    out = oracle.gemm(a, b, epi=epilogue, bias=bi, residual=r,
+                      out_dtype=np.float16 if out_dtype == torch.float16 else np.float32, nthreads=1)
+    return torch.from_numpy(out)
+
+
+def _worker(rank, world, port, M, N, K, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(7)  # identical full inputs on every rank
+        A = (torch.rand((M, K), generator=g) * 2 - 1).half()
+        B = (torch.rand((K, N), generator=g) * 2 - 1).half()
+        bias = torch.randn((N,), generator=g).half()
+        C_slab = local_slab_gemm(A, B, rank, world, epilogue="bias_gelu_tanh", bias=bias, gemm=_oracle_gemm)
+        C = gather_columns(C_slab)
+        if rank == 0:
+            q.put(C.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_split_and_gather_equal_single_rank(world):
+    M, N, K = 24, 64 * world, 40
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    C = None
+    deadline = time.time() + 180
+    while C is None and time.time() < deadline:
+        try:
+            C = q.get(timeout=1)
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in procs):
+                break
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert C is not None, f"ranks failed: {[p.exitcode for p in procs]}"
+    assert all(p.exitcode == 0 for p in procs)
+    g = torch.Generator().manual_seed(7)
+    A = (torch.rand((M, K), generator=g) * 2 - 1).half()
+    B = (torch.rand((K, N), generator=g) * 2 - 1).half()
+    bias = torch.randn((N,), generator=g).half()
+    full = oracle.gemm(A.numpy(), B.numpy(), epi="bias_gelu_tanh", bias=bias.numpy(), out_dtype=np.float16)
+    assert np.array_equal(C.view(np.uint16), full.view(np.uint16))
