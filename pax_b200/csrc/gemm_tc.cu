@@ -5,15 +5,19 @@
 
 namespace pax {
 
-pax_status_t launch_tc_f16(const Problem& p, int bn, cudaStream_t stream);
-pax_status_t launch_tc_f32(const Problem& p, int bn, cudaStream_t stream);
+pax_status_t launch_tc_f16(const Problem& p, int shape, cudaStream_t stream);
+pax_status_t launch_tc_f32(const Problem& p, int shape, cudaStream_t stream);
 int read_clear_device_error_tc_f16();
 int read_clear_device_error_tc_f32();
 
-size_t tc_smem_bytes(int bn, bool c_f16) {
-    if (bn == 256)
-        return c_f16 ? TcCfg<256, kStages256, __half>::SMEM_BYTES : TcCfg<256, kStages256, float>::SMEM_BYTES;
-    return c_f16 ? TcCfg<128, kStages128, __half>::SMEM_BYTES : TcCfg<128, kStages128, float>::SMEM_BYTES;
+size_t tc_smem_bytes(int shape, bool c_f16) {
+    if (shape == 2)
+        return c_f16 ? TcCfg<256, kStagesPair, __half, true>::SMEM_BYTES
+                     : TcCfg<256, kStagesPair, float, true>::SMEM_BYTES;
+    if (shape == 256)
+        return c_f16 ? TcCfg<256, kStages256, __half, false>::SMEM_BYTES
+                     : TcCfg<256, kStages256, float, false>::SMEM_BYTES;
+    return c_f16 ? TcCfg<128, kStages128, __half, false>::SMEM_BYTES : TcCfg<128, kStages128, float, false>::SMEM_BYTES;
 }
 
 int tc_pick_bn(long long M, long long N, int sms) {
@@ -26,9 +30,10 @@ int tc_pick_bn(long long M, long long N, int sms) {
     return 128;
 }
 
-pax_status_t launch_tc(const Problem& p, int bn, cudaStream_t stream) {
+pax_status_t launch_tc(const Problem& p, int shape, cudaStream_t stream) {
     if (p.M > 0x7fffffffLL || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
-    return p.c_f16 ? launch_tc_f16(p, bn == 256 ? 256 : 128, stream) : launch_tc_f32(p, bn == 256 ? 256 : 128, stream);
+    if (shape != 2 && shape != 256) shape = 128;
+    return p.c_f16 ? launch_tc_f16(p, shape, stream) : launch_tc_f32(p, shape, stream);
 }
 
 int read_clear_device_error_tc() {

@@ -43,11 +43,21 @@ struct TcParams {
     EpiParams epi;
 };
 
-template <int BN_, int STAGES_, typename OutT>
+// Tile configuration.  PAIR = false: one CTA computes a 128 x BN tile with
+// tcgen05.mma.cta_group::1.  PAIR = true: a cluster of two CTAs computes a
+// 256 x BN tile with tcgen05.mma.cta_group::2 issued by the even CTA; each
+// CTA stages its own 128 rows of A and BN/2 columns of B, and holds its 128
+// rows of the accumulator in its own TMEM.
+template <int BN_, int STAGES_, typename OutT, bool PAIR_>
 struct TcCfg {
-    static constexpr int BM = 128, BN = BN_, BK = 64, STAGES = STAGES_;
-    static constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KiB
-    static constexpr uint32_t B_BYTES = BN * BK * 2;  // 16 / 32 KiB
+    static constexpr bool PAIR = PAIR_;
+    static constexpr int BM = 128;                       // rows per CTA
+    static constexpr int BN = BN_;                       // accumulator columns (MMA N)
+    static constexpr int BN_LOCAL = PAIR ? BN / 2 : BN;  // B columns staged per CTA
+    static constexpr int TILE_M = PAIR ? 2 * BM : BM;    // rows per output tile
+    static constexpr int BK = 64, STAGES = STAGES_;
+    static constexpr uint32_t A_BYTES = BM * BK * 2;        // 16 KiB
+    static constexpr uint32_t B_BYTES = BN_LOCAL * BK * 2;  // 16 / 32 KiB
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_COLS = 128 / (int)sizeof(OutT);  // one 128-byte row per chunk
     static constexpr uint32_t STG_BYTES = 32 * 128;            // per warp, per buffer
@@ -56,9 +66,10 @@ struct TcCfg {
     static constexpr uint32_t NUM_BARS = 2 * STAGES + 5;
     static constexpr size_t SMEM_BYTES =
         1024 + (size_t)STAGES * STAGE_BYTES + STG_TOTAL + NUM_BARS * 8 + 16;
-    static constexpr uint32_t IDESC = umma_idesc_f16(BM, BN, /*a_mn*/ false, /*b_mn*/ true);
+    static constexpr uint32_t IDESC = umma_idesc_f16(PAIR ? 256 : 128, BN, /*a_mn*/ false, /*b_mn*/ true);
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+    static_assert(BN_LOCAL % 64 == 0, "B is staged in 64-column boxes");
 };
 
 __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& mb, int& nb) {
@@ -71,11 +82,11 @@ __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& mb, i
     nb = r / gm;
 }
 
-template <int BN, int STAGES, typename OutT, int RES, int GELU>
+template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const TcParams p) {
-    using Cfg = TcCfg<BN, STAGES, OutT>;
+    using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem =
         reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -95,6 +106,11 @@ __global__ void __launch_bounds__(192, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // Pair bookkeeping: rank within the CTA pair, index of the pair, number of pairs.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const bool leader = rank == 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -103,7 +119,8 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull0 + 8u * b, 1);
-            mbar_init(tempty0 + 8u * b, 4);  // one arrive per epilogue warp
+            // one arrive per epilogue warp (of both CTAs in pair mode)
+            mbar_init(tempty0 + 8u * b, PAIR ? 8 : 4);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -115,11 +132,15 @@ __global__ void __launch_bounds__(192, 1)
         tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
-        tmem_alloc<1>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
-        tmem_relinquish<1>();
+        tmem_alloc<PAIR ? 2 : 1>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+        tmem_relinquish<PAIR ? 2 : 1>();
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) {
+        cluster_sync();  // barrier initialisation visible to the peer CTA
+    } else {
+        __syncthreads();
+    }
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int num_kb = (p.K + Cfg::BK - 1) / Cfg::BK;
@@ -131,21 +152,35 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t phase = 0;
             bool ok = true;
             uint32_t issued = 0, last_parity = 0;
-            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+            for (int t = unit; ok && t < p.num_tiles; t += units) {
                 int mb, nb;
                 tile_coords(t, p, mb, nb);
+                const int arow = mb * Cfg::TILE_M + (int)rank * Cfg::BM;
+                const int bcol = nb * BN + (int)rank * Cfg::BN_LOCAL;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
                         ok = false;
                         break;
                     }
                     const uint32_t fb = full0 + 8u * stage;
-                    mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
-                    tma_load_2d(smem_u32(sA + stage * Cfg::A_BYTES), &tmA, fb, kb * Cfg::BK, mb * Cfg::BM);
+                    const uint32_t adst = smem_u32(sA + stage * Cfg::A_BYTES);
+                    const uint32_t bdst = smem_u32(sB + stage * Cfg::B_BYTES);
+                    if constexpr (PAIR) {
+                        // Both CTAs' loads complete on the leader's full barrier;
+                        // the leader announces the bytes of both.
+                        const uint32_t fb_leader = mapa_shared(fb, 0);
+                        if (leader) mbar_arrive_expect_tx(fb, 2 * Cfg::STAGE_BYTES);
+                        tma_load_2d_pair(adst, &tmA, fb_leader, kb * Cfg::BK, arow);
 #pragma unroll
-                    for (int j = 0; j < BN / 64; ++j)
-                        tma_load_2d(smem_u32(sB + stage * Cfg::B_BYTES + j * 8192), &tmB, fb,
-                                    nb * BN + j * 64, kb * Cfg::BK);
+                        for (int j = 0; j < Cfg::BN_LOCAL / 64; ++j)
+                            tma_load_2d_pair(bdst + j * 8192, &tmB, fb_leader, bcol + j * 64, kb * Cfg::BK);
+                    } else {
+                        mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+                        tma_load_2d(adst, &tmA, fb, kb * Cfg::BK, arow);
+#pragma unroll
+                        for (int j = 0; j < Cfg::BN_LOCAL / 64; ++j)
+                            tma_load_2d(bdst + j * 8192, &tmB, fb, bcol + j * 64, kb * Cfg::BK);
+                    }
                     issued |= 1u << stage;
                     last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
@@ -156,20 +191,28 @@ __global__ void __launch_bounds__(192, 1)
             }
             if (!ok) {
                 // Abort: every TMA load issued must land before the CTA exits.
-                for (int s = 0; s < STAGES; ++s)
-                    if (issued & (1u << s)) mbar_wait(full0 + 8u * s, (last_parity >> s) & 1u, nullptr);
+                if (!PAIR || leader) {
+                    for (int s = 0; s < STAGES; ++s)
+                        if (issued & (1u << s)) mbar_wait(full0 + 8u * s, (last_parity >> s) & 1u, nullptr);
+                } else {
+                    // The peer's loads complete on the leader's barriers, which
+                    // this CTA cannot wait on: give them ample time to land.
+                    const unsigned long long t0 = globaltimer_ns();
+                    while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+                }
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // ------------------------------------------------ MMA issuer (leader only in pair mode)
+        if (lane == 0 && leader) {
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-                if (!mbar_wait(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
+            for (int t = unit; ok && t < p.num_tiles; t += units) {
+                // In pair mode the releases come from both CTAs' epilogues.
+                if (!mbar_wait<PAIR>(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
                 for (int kb = 0; kb < num_kb; ++kb) {
@@ -184,39 +227,55 @@ __global__ void __launch_bounds__(192, 1)
                     for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
                         const uint64_t ad = umma_desc_sw128(a0 + kk * 32, 16, 1024);
                         const uint64_t bd = umma_desc_sw128(b0 + kk * 2048, 8192, 1024);
-                        tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (kb | kk) != 0 ? 1u : 0u);
+                        if constexpr (PAIR)
+                            tc_mma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, (kb | kk) != 0 ? 1u : 0u);
+                        else
+                            tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (kb | kk) != 0 ? 1u : 0u);
                     }
-                    tc_commit(empty0 + 8u * stage);
+                    if constexpr (PAIR) {
+                        tc_commit_pair(mapa_shared(empty0 + 8u * stage, 0));
+                        tc_commit_pair(mapa_shared(empty0 + 8u * stage, 1));
+                    } else {
+                        tc_commit(empty0 + 8u * stage);
+                    }
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
-                tc_commit(tfull0 + 8u * acc);
+                if constexpr (PAIR) {
+                    tc_commit_pair(mapa_shared(tfull0 + 8u * acc, 0));
+                    tc_commit_pair(mapa_shared(tfull0 + 8u * acc, 1));
+                } else {
+                    tc_commit(tfull0 + 8u * acc);
+                }
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1u;
                 }
             }
-            // No MMA may still be writing TMEM when it is released.
-            tc_commit(drain_bar);
+            // No MMA may still be writing TMEM (or reading either CTA's shared
+            // memory) when the pair tears down.
+            if constexpr (PAIR)
+                tc_commit_pair(mapa_shared(drain_bar, 0));
+            else
+                tc_commit(drain_bar);
             mbar_wait(drain_bar, 0, nullptr);
         }
     } else {
         // ------------------------------------------------ epilogue warps
         constexpr int EC = Cfg::EPI_COLS;
-        constexpr int NCH = BN / EC;
         const int q = warp & 3;  // TMEM lane quarter this warp may read
         uint8_t* stg = sStg + (warp - 2) * 2 * Cfg::STG_BYTES;
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+        for (int t = unit; t < p.num_tiles; t += units) {
             int mb, nb;
             tile_coords(t, p, mb, nb);
-            const long long row = (long long)mb * Cfg::BM + q * 32 + lane;
+            const int row0 = mb * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
+            const long long row = (long long)row0 + lane;
             const long long tcol0 = (long long)nb * BN;
-            const int row0 = mb * Cfg::BM + q * 32;
             // Operands that do not depend on the accumulator are fetched before
             // waiting for it: this tile's bias and the first residual chunk.
             const uint4 bias8 = bias_tile_load(tcol0, BN, lane, p.N, p.epi);
@@ -227,28 +286,41 @@ __global__ void __launch_bounds__(192, 1)
             if (!ok) break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+            // Chunks wholly outside C (beyond N, or this warp's 32 rows beyond
+            // M) are neither read nor stored.
+            const long long valid_cols = p.N - tcol0 < BN ? p.N - tcol0 : BN;
+            const int nch = row0 < p.M ? (int)((valid_cols + EC - 1) / EC) : 0;
+            auto release_accumulator = [&]() {
+                // Whole accumulator read: hand it back to the MMA warp (of the
+                // pair leader).
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if (PAIR && !leader)
+                        mbar_arrive_cluster(tempty0 + 8u * acc, 0);
+                    else
+                        mbar_arrive(tempty0 + 8u * acc);
+                }
+            };
+            if (nch == 0) release_accumulator();
 #pragma unroll 1
-            for (int ci = 0; ci < NCH; ++ci) {
+            for (int ci = 0; ci < nch; ++ci) {
                 const int c = ci * EC;
                 float v[EC];
                 tmem_ld_32x32b_x32(t_row + (uint32_t)c, v);
                 if constexpr (EC == 64) tmem_ld_32x32b_x32(t_row + (uint32_t)c + 32u, v + 32);
                 tmem_wait_ld();
-                if (ci == NCH - 1) {
-                    // Whole accumulator read: hand it back to the MMA warp.
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(tempty0 + 8u * acc);
-                }
+                if (ci == nch - 1) release_accumulator();
                 epi_linear<EC, RES>(v, rc, bias8, c, p.epi);
                 // The residual registers are free again: start the next
                 // chunk's loads, which then overlap the GeLU math below.
                 if constexpr (RES != 0) {
-                    if (ci + 1 < NCH) res_prefetch<EC, RES>(rc, row, tcol0 + c + EC, p.M, p.N, p.epi);
+                    if (ci + 1 < nch) res_prefetch<EC, RES>(rc, row, tcol0 + c + EC, p.M, p.N, p.epi);
                 }
                 epi_gelu<EC, GELU>(v);
                 // Staging buffer (ci & 1) is free once at most one store group
-                // (the one using the other buffer) is still reading it.
+                // (the previous chunk's, using the other buffer) is still
+                // reading; every processed chunk commits exactly one group.
                 if (lane == 0) bulk_wait_read<1>();
                 __syncwarp();
                 uint8_t* sbuf = stg + (ci & 1) * Cfg::STG_BYTES;
@@ -272,9 +344,8 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                const long long col0 = tcol0 + c;
-                if (lane == 0 && col0 < p.N && row0 < p.M) {  // boxes wholly outside C are skipped
-                    tma_store_2d(&tmC, smem_u32(sbuf), (int)col0, row0);
+                if (lane == 0) {
+                    tma_store_2d(&tmC, smem_u32(sbuf), (int)(tcol0 + c), row0);
                     bulk_commit();
                 }
             }
@@ -289,10 +360,14 @@ __global__ void __launch_bounds__(192, 1)
 
     __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) {
+        cluster_sync();  // neither CTA leaves while the pair's MMAs or arrivals may touch it
+    } else {
+        __syncthreads();
+    }
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc<1>(tmem_base, Cfg::TMEM_COLS);
+        tmem_dealloc<PAIR ? 2 : 1>(tmem_base, Cfg::TMEM_COLS);
     }
 }
 
@@ -330,9 +405,9 @@ static bool make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, 
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, typename OutT, int RES, int GELU>
+template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
 static pax_status_t launch_tc_impl(const Problem& pr, cudaStream_t stream) {
-    using Cfg = TcCfg<BN, STAGES, OutT>;
+    using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     const bool f16 = sizeof(OutT) == 2;
     CUtensorMap tA, tB, tC;
     if (!make_tmap(&tA, pr.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pr.K, pr.M, pr.lda * 2, 64, 128)) return PAX_ERR_CUDA;
@@ -345,46 +420,75 @@ static pax_status_t launch_tc_impl(const Problem& pr, cudaStream_t stream) {
     p.M = (int)pr.M;
     p.N = (int)pr.N;
     p.K = (int)pr.K;
-    p.tiles_m = (int)((pr.M + Cfg::BM - 1) / Cfg::BM);
+    p.tiles_m = (int)((pr.M + Cfg::TILE_M - 1) / Cfg::TILE_M);
     p.tiles_n = (int)((pr.N + BN - 1) / BN);
     p.num_tiles = p.tiles_m * p.tiles_n;
-    p.group_m = 8;
+    p.group_m = PAIR ? 8 : 16;
     p.epi = pr.epi;
 
     const int dev = current_device();
     const int sms = device_sm_count(dev);
-    auto kern = gemm_tc_kernel<BN, STAGES, OutT, RES, GELU>;
+    auto kern = gemm_tc_kernel<BN, STAGES, OutT, RES, GELU, PAIR>;
     // Attribute is per device; setting it again is cheap and idempotent.
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES) != cudaSuccess)
         return PAX_ERR_CUDA;
-    const int grid = p.num_tiles < sms ? p.num_tiles : sms;
-    kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(tA, tB, tC, p);
+    if constexpr (PAIR) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.blockDim = dim3(192);
+        cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cfg.gridDim = dim3(2 * 74);
+        // Pairs that can be resident at once (SMs pair up within a GPC).
+        static int max_pairs[64] = {0};
+        int& mp = max_pairs[dev & 63];
+        if (mp == 0) {
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = sms / 2;
+            mp = n;
+        }
+        const int pairs = p.num_tiles < mp ? p.num_tiles : mp;
+        cfg.gridDim = dim3(2 * pairs);
+        if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p) != cudaSuccess) return PAX_ERR_CUDA;
+    } else {
+        const int grid = p.num_tiles < sms ? p.num_tiles : sms;
+        kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(tA, tB, tC, p);
+    }
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }
 
 constexpr int kStages256 = 4;
 constexpr int kStages128 = 6;
+constexpr int kStagesPair = 6;
 
 // Residual type and GeLU form are compile-time parameters so that each
 // instantiation carries only the epilogue code it runs.
-template <int BN, int STAGES, typename OutT, int GELU>
+template <int BN, int STAGES, typename OutT, int GELU, bool PAIR>
 static pax_status_t launch_tc_gelu(const Problem& p, cudaStream_t stream) {
-    if (!(p.epi.flags & EPI_RES)) return launch_tc_impl<BN, STAGES, OutT, 0, GELU>(p, stream);
-    if (p.epi.flags & EPI_RES_F32) return launch_tc_impl<BN, STAGES, OutT, 2, GELU>(p, stream);
-    return launch_tc_impl<BN, STAGES, OutT, 1, GELU>(p, stream);
+    if (!(p.epi.flags & EPI_RES)) return launch_tc_impl<BN, STAGES, OutT, 0, GELU, PAIR>(p, stream);
+    if (p.epi.flags & EPI_RES_F32) return launch_tc_impl<BN, STAGES, OutT, 2, GELU, PAIR>(p, stream);
+    return launch_tc_impl<BN, STAGES, OutT, 1, GELU, PAIR>(p, stream);
 }
 
-template <int BN, int STAGES, typename OutT>
+template <int BN, int STAGES, typename OutT, bool PAIR>
 static pax_status_t launch_tc_res(const Problem& p, cudaStream_t stream) {
-    if (p.epi.flags & EPI_GELU_TANH) return launch_tc_gelu<BN, STAGES, OutT, 1>(p, stream);
-    if (p.epi.flags & EPI_GELU_ERF) return launch_tc_gelu<BN, STAGES, OutT, 2>(p, stream);
-    return launch_tc_gelu<BN, STAGES, OutT, 0>(p, stream);
+    if (p.epi.flags & EPI_GELU_TANH) return launch_tc_gelu<BN, STAGES, OutT, 1, PAIR>(p, stream);
+    if (p.epi.flags & EPI_GELU_ERF) return launch_tc_gelu<BN, STAGES, OutT, 2, PAIR>(p, stream);
+    return launch_tc_gelu<BN, STAGES, OutT, 0, PAIR>(p, stream);
 }
 
+// shape: 128 / 256 = one CTA per 128 x shape tile; 2 = CTA pair, 256 x 256 tile.
 template <typename OutT>
-static pax_status_t launch_tc_typed(const Problem& p, int bn, cudaStream_t stream) {
-    if (bn == 256) return launch_tc_res<256, kStages256, OutT>(p, stream);
-    return launch_tc_res<128, kStages128, OutT>(p, stream);
+static pax_status_t launch_tc_typed(const Problem& p, int shape, cudaStream_t stream) {
+    if (shape == 2) return launch_tc_res<256, kStagesPair, OutT, true>(p, stream);
+    if (shape == 256) return launch_tc_res<256, kStages256, OutT, false>(p, stream);
+    return launch_tc_res<128, kStages128, OutT, false>(p, stream);
 }
 
 static int read_clear_device_error_this_unit() {

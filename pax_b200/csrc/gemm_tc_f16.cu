@@ -3,8 +3,8 @@
 
 namespace pax {
 
-pax_status_t launch_tc_f16(const Problem& p, int bn, cudaStream_t stream) {
-    return launch_tc_typed<__half>(p, bn, stream);
+pax_status_t launch_tc_f16(const Problem& p, int shape, cudaStream_t stream) {
+    return launch_tc_typed<__half>(p, shape, stream);
 }
 
 int read_clear_device_error_tc_f16() { return read_clear_device_error_this_unit(); }

@@ -222,12 +222,16 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
     if (algo == PAX_ALGO_AUTO) algo = select_algo(p);
     pax_status_t st;
     switch (algo) {
-        case PAX_ALGO_TC:
-        case PAX_ALGO_TC2: {
+        case PAX_ALGO_TC: {
             if (!tma_compatible(p)) return fail(PAX_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned rows");
             int bn = env_int("PAX_TC_BN", 0);
             if (bn != 128 && bn != 256) bn = tc_pick_bn(p.M, p.N, di.sms);
             st = launch_tc(p, bn, s);
+            break;
+        }
+        case PAX_ALGO_TC2: {
+            if (!tma_compatible(p)) return fail(PAX_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned rows");
+            st = launch_tc(p, 2, s);
             break;
         }
         case PAX_ALGO_SKINNY: {

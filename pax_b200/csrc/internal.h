@@ -30,7 +30,9 @@ int current_device();
 bool tma_compatible(const Problem& p);
 
 // Launchers.  Each returns PAX_OK or an error status; none synchronises.
-pax_status_t launch_tc(const Problem& p, int bn, cudaStream_t stream);
+// launch_tc shape: 128 or 256 = one CTA per 128 x shape output tile,
+// 2 = CTA pair (cluster of two, tcgen05 cta_group::2) per 256 x 256 tile.
+pax_status_t launch_tc(const Problem& p, int shape, cudaStream_t stream);
 pax_status_t launch_simt(const Problem& p, cudaStream_t stream);
 // Skinny kernel: `ws` holds grid*2*MP*128 fp32 partial sums and `counters`
 // one int per 128-column tile, zero before the launch (the kernel leaves
@@ -39,8 +41,8 @@ void skinny_geometry(long long M, long long N, long long K, int sms, int* grid, 
                      size_t* counter_bytes);
 pax_status_t launch_skinny_ws(const Problem& p, int grid, float* ws, int* counters, cudaStream_t stream);
 
-// Dynamic shared memory of the tcgen05 kernel for a tile width / output type.
-size_t tc_smem_bytes(int bn, bool c_f16);
+// Dynamic shared memory of the tcgen05 kernel for a tile shape / output type.
+size_t tc_smem_bytes(int shape, bool c_f16);
 // Tile width launch_tc picks for a problem when none is forced.
 int tc_pick_bn(long long M, long long N, int sms);
 // Largest M the skinny kernel accepts.

@@ -51,6 +51,18 @@ def test_tc_plain(cuda, rng, monkeypatch, bn, shape, out):
     check(got, oracle.gemm(A, B, out_dtype=out), out)
 
 
+@pytest.mark.parametrize("shape", [(256, 256, 64), (512, 768, 512), (300, 520, 200), (128, 256, 128), (1000, 8, 8),
+                                   (384, 264, 4104)])
+@pytest.mark.parametrize("out", [np.float32, np.float16])
+def test_tc2_cta_pair(cuda, rng, shape, out):
+    """256 x 256 tiles on CTA pairs (tcgen05 cta_group::2), ragged edges
+    included (rows of the odd CTA wholly outside C when M <= 128)."""
+    M, N, K = shape
+    A, B = inputs(rng, M, N, K)
+    got = run_gemm(A, B, cuda, out_dtype=out, algo="tc2")
+    check(got, oracle.gemm(A, B, out_dtype=out), out)
+
+
 @pytest.mark.parametrize("shape", [(300, 520, 200), (129, 264, 72), (1000, 8, 8), (65, 1032, 136), (77, 40, 4104)])
 @pytest.mark.parametrize("out", [np.float32, np.float16])
 def test_tc_ragged_edges(cuda, rng, shape, out):
@@ -67,7 +79,8 @@ EPIS = ["none", "bias", "bias_gelu_tanh", "bias_gelu_erf", "residual_gelu_tanh",
 @pytest.mark.parametrize("epi", EPIS)
 @pytest.mark.parametrize("out", [np.float32, np.float16])
 @pytest.mark.parametrize("res_dtype", [np.float32, np.float16])
-def test_tc_epilogues(cuda, rng, epi, out, res_dtype):
+@pytest.mark.parametrize("algo", ["tc", "tc2"])
+def test_tc_epilogues(cuda, rng, epi, out, res_dtype, algo):
     if "residual" not in epi and res_dtype == np.float16:
         pytest.skip("residual dtype irrelevant")
     M, N, K = 256, 520, 320
@@ -75,12 +88,12 @@ def test_tc_epilogues(cuda, rng, epi, out, res_dtype):
     bias = rng.standard_normal(N).astype(np.float16)
     res = rng.standard_normal((M, N)).astype(res_dtype)
     got = run_gemm(A, B, cuda, epi=epi, out_dtype=out, bias=bias if "bias" in epi else None,
-                   residual=res if "residual" in epi else None, algo="tc")
+                   residual=res if "residual" in epi else None, algo=algo)
     ref = oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out)
     check(got, ref, out)
 
 
-@pytest.mark.parametrize("algo", ["tc", "skinny", "simt"])
+@pytest.mark.parametrize("algo", ["tc", "tc2", "skinny", "simt"])
 def test_scale_bias_gelu(cuda, rng, algo):
     M = 48 if algo == "skinny" else 200
     A, B = inputs(rng, M, 264, 192)
@@ -135,13 +148,15 @@ def test_simt_unaligned(cuda, rng, shape, epi):
 
 
 # ---------------------------------------------------------------- exactness
-@pytest.mark.parametrize("algo,M", [("tc", 256), ("skinny", 16), ("simt", 256)])
+@pytest.mark.parametrize("algo,M", [("tc", 256), ("tc2", 384), ("skinny", 16), ("simt", 256)])
 def test_integer_inputs_bit_exact(cuda, rng, algo, M):
     A = rng.integers(-3, 4, (M, 512)).astype(np.float16)
     B = rng.integers(-3, 4, (512, 384)).astype(np.float16)
     got = run_gemm(A, B, cuda, out_dtype=np.float32, algo=algo)
     exact = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.float32)
-    assert np.array_equal(got, exact)
+    bad = np.argwhere(got != exact)
+    assert bad.size == 0, (f"{len(bad)} mismatches, first {bad[:8].tolist()}, "
+                           f"got {got[tuple(bad[0])]} want {exact[tuple(bad[0])]}")
 
 
 GOLDEN = sorted(glob.glob(os.path.join(ROOT, "tests", "golden", "gemm_*.npz")))
@@ -298,7 +313,7 @@ def test_gelu_bound_on_device(cuda, rng):
     assert (np.abs(t - e) <= 1e-3 * np.abs(x) + 1e-6).all()
 
 
-@pytest.mark.parametrize("algo,M", [("tc", 1024), ("skinny", 16)])
+@pytest.mark.parametrize("algo,M", [("tc", 1024), ("tc2", 1024), ("skinny", 16)])
 def test_deterministic(cuda, rng, algo, M):
     N, K = 4096, 2048
     A, B = inputs(rng, M, N, K)
