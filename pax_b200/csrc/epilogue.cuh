@@ -31,6 +31,20 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return 0.5f * x * (1.0f + tanhf(k_alpha * (x + k_beta * x * x * x)));
 }
 
+// tanh form with the hardware tanh.approx.f32 (one transcendental-pipe op,
+// relative error about 2^-11).  GeLU error <= 0.5|x| * 2^-11 ~ 2.4e-4 |x|,
+// below the rounding of an fp16 result; used only when C is fp16.
+__device__ __forceinline__ float tanh_hw(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float gelu_tanh_hw(float x) {
+    const float k_alpha = 0.7978845608028654f;  // sqrt(2/pi)
+    const float k_beta = 0.044715f;
+    return 0.5f * x * (1.0f + tanh_hw(k_alpha * (x + k_beta * x * x * x)));
+}
+
 __device__ __forceinline__ float gelu_erf(float x) {
     return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
@@ -136,7 +150,7 @@ __device__ __forceinline__ uint4 bias_tile_load(long long tile_col0, int tile_co
 // Epilogue of one row chunk of n columns starting at tile column `tc` (a
 // multiple of 8), in two phases so the caller can refill `rc` in between:
 //   epi_linear: v = alpha*v (+ bias[j]) (+ R[i][j])
-//   epi_gelu:   v = GeLU(v)                     GELU: 0 none, 1 tanh, 2 erf
+//   epi_gelu:   v = GeLU(v)     GELU: 0 none, 1 tanh (tanhf), 2 erf, 3 tanh (tanh.approx)
 // `bias8` is this lane's bias_tile_load value.
 template <int n, int RES>
 __device__ __forceinline__ void epi_linear(float (&v)[n], const ResChunk<n, RES>& rc, uint4 bias8, int tc,
@@ -185,6 +199,9 @@ __device__ __forceinline__ void epi_gelu(float (&v)[n]) {
     if constexpr (GELU == 1) {
 #pragma unroll
         for (int i = 0; i < n; ++i) v[i] = gelu_tanh(v[i]);
+    } else if constexpr (GELU == 3) {
+#pragma unroll
+        for (int i = 0; i < n; ++i) v[i] = gelu_tanh_hw(v[i]);
     } else if constexpr (GELU == 2) {
 #pragma unroll
         for (int i = 0; i < n; ++i) v[i] = gelu_erf(v[i]);

@@ -30,6 +30,20 @@ int tc_pick_bn(long long M, long long N, int sms) {
     return 128;
 }
 
+// Tile shape by a wave-count cost model.  Time ~ waves x (work of one tile
+// per SM) / (relative per-SM throughput of the shape); the throughputs are
+// measured ratios on B200 (128x256 tiles = 1, CTA-pair 256x256 = 1.04,
+// 128x128 = 0.67).
+int tc_pick_shape(long long M, long long N, int sms) {
+    const long long pairs = sms / 2;
+    auto waves = [](long long tiles, long long units) { return (tiles + units - 1) / units; };
+    const double t256 = (double)waves(((M + 127) / 128) * ((N + 255) / 256), sms) * 1.0;
+    const double t128 = (double)waves(((M + 127) / 128) * ((N + 127) / 128), sms) * 0.5 / 0.67;
+    const double tpair = (double)waves(((M + 255) / 256) * ((N + 255) / 256), pairs) * 1.0 / 1.04;
+    if (tpair <= t256 && tpair <= t128) return 2;
+    return t256 <= t128 ? 256 : 128;
+}
+
 pax_status_t launch_tc(const Problem& p, int shape, cudaStream_t stream) {
     if (p.M > 0x7fffffffLL || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
     if (shape != 2 && shape != 256) shape = 128;

@@ -210,6 +210,10 @@ __global__ void __launch_bounds__(192, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
+            // Descriptors of stage 0, k-step 0; other stages / k-steps differ
+            // only in the start-address field (address >> 4 in the low bits).
+            const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA), 16, 1024);
+            const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB), 8192, 1024);
             for (int t = unit; ok && t < p.num_tiles; t += units) {
                 // In pair mode the releases come from both CTAs' epilogues.
                 if (!mbar_wait<PAIR>(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
@@ -221,12 +225,12 @@ __global__ void __launch_bounds__(192, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + stage * Cfg::A_BYTES);
-                    const uint32_t b0 = smem_u32(sB + stage * Cfg::B_BYTES);
+                    const uint64_t as = adesc0 + (uint64_t)((stage * Cfg::A_BYTES) >> 4);
+                    const uint64_t bs = bdesc0 + (uint64_t)((stage * Cfg::B_BYTES) >> 4);
 #pragma unroll
                     for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
-                        const uint64_t ad = umma_desc_sw128(a0 + kk * 32, 16, 1024);
-                        const uint64_t bd = umma_desc_sw128(b0 + kk * 2048, 8192, 1024);
+                        const uint64_t ad = as + (uint64_t)((kk * 32) >> 4);    // +32 B along K
+                        const uint64_t bd = bs + (uint64_t)((kk * 2048) >> 4);  // +16 rows of K
                         if constexpr (PAIR)
                             tc_mma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, (kb | kk) != 0 ? 1u : 0u);
                         else
@@ -478,7 +482,10 @@ static pax_status_t launch_tc_gelu(const Problem& p, cudaStream_t stream) {
 
 template <int BN, int STAGES, typename OutT, bool PAIR>
 static pax_status_t launch_tc_res(const Problem& p, cudaStream_t stream) {
-    if (p.epi.flags & EPI_GELU_TANH) return launch_tc_gelu<BN, STAGES, OutT, 1, PAIR>(p, stream);
+    // GeLU-tanh uses the hardware tanh when the result is rounded to fp16
+    // anyway, and tanhf for fp32 results.
+    if (p.epi.flags & EPI_GELU_TANH)
+        return launch_tc_gelu<BN, STAGES, OutT, sizeof(OutT) == 2 ? 3 : 1, PAIR>(p, stream);
     if (p.epi.flags & EPI_GELU_ERF) return launch_tc_gelu<BN, STAGES, OutT, 2, PAIR>(p, stream);
     return launch_tc_gelu<BN, STAGES, OutT, 0, PAIR>(p, stream);
 }

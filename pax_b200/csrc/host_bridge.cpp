@@ -219,12 +219,21 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
     const DevInfo di = device_info(dev);
     if (di.major != 10) return fail(PAX_ERR_NO_DEVICE, "device %d is sm_%d%d; this library needs sm_100", dev,
                                     di.major, di.minor);
-    if (algo == PAX_ALGO_AUTO) algo = select_algo(p);
+    int shape = 0;  // tensor-core tile shape, when chosen here
+    if (algo == PAX_ALGO_AUTO) {
+        algo = select_algo(p);
+        if (algo == PAX_ALGO_TC) {
+            shape = tc_pick_shape(p.M, p.N, di.sms);
+            const int forced = env_int("PAX_TC_SHAPE", 0);
+            if (forced == 2 || forced == 128 || forced == 256) shape = forced;
+            if (shape == 2) algo = PAX_ALGO_TC2;
+        }
+    }
     pax_status_t st;
     switch (algo) {
         case PAX_ALGO_TC: {
             if (!tma_compatible(p)) return fail(PAX_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned rows");
-            int bn = env_int("PAX_TC_BN", 0);
+            int bn = shape ? shape : env_int("PAX_TC_BN", 0);
             if (bn != 128 && bn != 256) bn = tc_pick_bn(p.M, p.N, di.sms);
             st = launch_tc(p, bn, s);
             break;
@@ -327,7 +336,15 @@ pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc) {
     Problem p;
     if (normalize(desc, &p) != PAX_OK) return PAX_ALGO_AUTO;
     set_status(PAX_OK);
-    return select_algo(p);
+    pax_algo_t a = select_algo(p);
+    // With a device present, report the tensor-core tile shape as well.
+    int dev = 0, sms = 0;
+    if (a == PAX_ALGO_TC && cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0 &&
+        tc_pick_shape(p.M, p.N, sms) == 2)
+        a = PAX_ALGO_TC2;
+    cudaGetLastError();  // no device here is not an error of this call
+    return a;
 }
 
 // ======================================================= reference launchers

@@ -43,8 +43,10 @@ pax_status_t launch_skinny_ws(const Problem& p, int grid, float* ws, int* counte
 
 // Dynamic shared memory of the tcgen05 kernel for a tile shape / output type.
 size_t tc_smem_bytes(int shape, bool c_f16);
-// Tile width launch_tc picks for a problem when none is forced.
+// Tile width of the one-CTA shape for a problem (128 or 256).
 int tc_pick_bn(long long M, long long N, int sms);
+// Tile shape pax_gemm_ex picks by itself: 128, 256 (one CTA) or 2 (pair).
+int tc_pick_shape(long long M, long long N, int sms);
 // Largest M the skinny kernel accepts.
 constexpr long long kSkinnyMaxM = 64;
 

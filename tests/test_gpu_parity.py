@@ -313,6 +313,19 @@ def test_gelu_bound_on_device(cuda, rng):
     assert (np.abs(t - e) <= 1e-3 * np.abs(x) + 1e-6).all()
 
 
+@pytest.mark.parametrize("algo", ["tc", "tc2"])
+def test_gelu_bound_on_device_fp16(cuda, rng, algo):
+    """fp16 results (hardware tanh in the GeLU-tanh epilogue): the bound holds
+    up to the fp16 rounding of the two outputs compared."""
+    M, N, K = 512, 512, 512
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    x = run_gemm(A, B, cuda, epi="bias", bias=bias, out_dtype=np.float32, algo=algo)
+    t = run_gemm(A, B, cuda, epi="bias_gelu_tanh", bias=bias, out_dtype=np.float16, algo=algo).astype(np.float32)
+    e = run_gemm(A, B, cuda, epi="bias_gelu_erf", bias=bias, out_dtype=np.float16, algo=algo).astype(np.float32)
+    assert (np.abs(t - e) <= 1e-3 * np.abs(x) + 2.0 ** -10 * (np.abs(t) + np.abs(e)) + 1e-6).all()
+
+
 @pytest.mark.parametrize("algo,M", [("tc", 1024), ("tc2", 1024), ("skinny", 16)])
 def test_deterministic(cuda, rng, algo, M):
     N, K = 4096, 2048
