@@ -40,8 +40,33 @@ struct TcParams {
     int M, N, K;
     int tiles_m, tiles_n, num_tiles;
     int group_m;  // output tiles are visited in column-major groups of group_m tile rows
+    // Work items: tiles [0, full_items) whole, then the last split_tiles
+    // tiles in two K halves each (the tail wave), so
+    // num_items = full_items + 2 * split_tiles.
+    int full_items, split_tiles, num_items;
+    float* ws;      // split partials: [split_tiles][2 halves][CTAs per tile][128][BN] fp32
+    int* counters;  // [split_tiles][CTAs per tile], zero between launches
     EpiParams epi;
 };
+
+// Work item -> output tile and k-block range [kb0, kb1); part = -1 for a
+// whole tile, else which K half of a split tile.
+__device__ __forceinline__ void tc_item(int item, const TcParams& p, int num_kb, int& tile, int& kb0, int& kb1,
+                                        int& part) {
+    if (item < p.full_items) {
+        tile = item;
+        kb0 = 0;
+        kb1 = num_kb;
+        part = -1;
+    } else {
+        const int j = item - p.full_items;
+        tile = p.full_items + (j >> 1);
+        part = j & 1;
+        const int h = num_kb >> 1;
+        kb0 = part ? h : 0;
+        kb1 = part ? num_kb : h;
+    }
+}
 
 // Tile configuration.  PAIR = false: one CTA computes a 128 x BN tile with
 // tcgen05.mma.cta_group::1.  PAIR = true: a cluster of two CTAs computes a
@@ -152,12 +177,14 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t phase = 0;
             bool ok = true;
             uint32_t issued = 0, last_parity = 0;
-            for (int t = unit; ok && t < p.num_tiles; t += units) {
+            for (int item = unit; ok && item < p.num_items; item += units) {
+                int t, kb0, kb1, part;
+                tc_item(item, p, num_kb, t, kb0, kb1, part);
                 int mb, nb;
                 tile_coords(t, p, mb, nb);
                 const int arow = mb * Cfg::TILE_M + (int)rank * Cfg::BM;
                 const int bcol = nb * BN + (int)rank * Cfg::BN_LOCAL;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
                         ok = false;
                         break;
@@ -214,12 +241,14 @@ __global__ void __launch_bounds__(192, 1)
             // only in the start-address field (address >> 4 in the low bits).
             const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA), 16, 1024);
             const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB), 8192, 1024);
-            for (int t = unit; ok && t < p.num_tiles; t += units) {
+            for (int item = unit; ok && item < p.num_items; item += units) {
+                int t, kb0, kb1, part;
+                tc_item(item, p, num_kb, t, kb0, kb1, part);
                 // In pair mode the releases come from both CTAs' epilogues.
                 if (!mbar_wait<PAIR>(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(full0 + 8u * stage, phase, abort_flag)) {
                         ok = false;
                         break;
@@ -232,9 +261,9 @@ __global__ void __launch_bounds__(192, 1)
                         const uint64_t ad = as + (uint64_t)((kk * 32) >> 4);    // +32 B along K
                         const uint64_t bd = bs + (uint64_t)((kk * 2048) >> 4);  // +16 rows of K
                         if constexpr (PAIR)
-                            tc_mma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, (kb | kk) != 0 ? 1u : 0u);
+                            tc_mma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
                         else
-                            tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (kb | kk) != 0 ? 1u : 0u);
+                            tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
                     }
                     if constexpr (PAIR) {
                         tc_commit_pair(mapa_shared(empty0 + 8u * stage, 0));
@@ -274,7 +303,10 @@ __global__ void __launch_bounds__(192, 1)
         uint8_t* stg = sStg + (warp - 2) * 2 * Cfg::STG_BYTES;
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int t = unit; t < p.num_tiles; t += units) {
+        volatile int* last_flag = abort_flag + 1;
+        for (int item = unit; item < p.num_items; item += units) {
+            int t, kb0, kb1, part;
+            tc_item(item, p, num_kb, t, kb0, kb1, part);
             int mb, nb;
             tile_coords(t, p, mb, nb);
             const int row0 = mb * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
@@ -286,7 +318,9 @@ __global__ void __launch_bounds__(192, 1)
             ResChunk<EC, RES> rc;
             res_prefetch<EC, RES>(rc, row, tcol0, p.M, p.N, p.epi);
             bool ok = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag);
-            ok = __all_sync(0xffffffffu, ok);
+            // Split items meet at named barriers below, so all four epilogue
+            // warps must take the same branch.
+            ok = part >= 0 ? named_barrier_and<1, 128>(ok) : __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
@@ -306,6 +340,47 @@ __global__ void __launch_bounds__(192, 1)
                         mbar_arrive(tempty0 + 8u * acc);
                 }
             };
+            // Split tile: park this half's fp32 sums, count in, and let the
+            // second half to arrive finish the tile with other + own.  Two
+            // fp32 terms commute, so the result does not depend on the order.
+            const float* other = nullptr;
+            if (part >= 0) {
+                const int sidx = (t - p.full_items) * (PAIR ? 2 : 1) + (int)rank;
+                const int row_local = q * 32 + lane;
+                float* mine = p.ws + ((size_t)(2 * sidx + part) * 128 + row_local) * BN;
+                if (row0 < p.M) {
+#pragma unroll 1
+                    for (int c = 0; c < (int)valid_cols; c += 32) {
+                        float w[32];
+                        tmem_ld_32x32b_x32(t_row + (uint32_t)c, w);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            __stcg(reinterpret_cast<float4*>(mine + c + i), make_float4(w[i], w[i + 1], w[i + 2], w[i + 3]));
+                    }
+                }
+                __threadfence();
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (warp == 2 && lane == 0) {
+                    const int prev = atomicAdd(p.counters + sidx, 1);
+                    const int is_last = prev == 1 ? 1 : 0;
+                    if (is_last) p.counters[sidx] = 0;  // ready for the next launch
+                    *last_flag = is_last;
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                const bool is_last = *last_flag != 0;
+                asm volatile("bar.sync 1, 128;" ::: "memory");  // flag read by all before reuse
+                if (!is_last) {
+                    release_accumulator();
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_phase ^= 1u;
+                    }
+                    continue;
+                }
+                __threadfence();
+                other = p.ws + ((size_t)(2 * sidx + (part ^ 1)) * 128 + row_local) * BN;
+            }
             if (nch == 0) release_accumulator();
 #pragma unroll 1
             for (int ci = 0; ci < nch; ++ci) {
@@ -315,6 +390,16 @@ __global__ void __launch_bounds__(192, 1)
                 if constexpr (EC == 64) tmem_ld_32x32b_x32(t_row + (uint32_t)c + 32u, v + 32);
                 tmem_wait_ld();
                 if (ci == nch - 1) release_accumulator();
+                if (other != nullptr) {
+#pragma unroll
+                    for (int i = 0; i < EC; i += 4) {
+                        const float4 o = __ldcg(reinterpret_cast<const float4*>(other + c + i));
+                        v[i] += o.x;
+                        v[i + 1] += o.y;
+                        v[i + 2] += o.z;
+                        v[i + 3] += o.w;
+                    }
+                }
                 epi_linear<EC, RES>(v, rc, bias8, c, p.epi);
                 // The residual registers are free again: start the next
                 // chunk's loads, which then overlap the GeLU math below.
@@ -410,7 +495,8 @@ static bool make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, 
 }
 
 template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
-static pax_status_t launch_tc_impl(const Problem& pr, cudaStream_t stream) {
+static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, float* ws, int* counters,
+                                   cudaStream_t stream) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     const bool f16 = sizeof(OutT) == 2;
     CUtensorMap tA, tB, tC;
@@ -428,10 +514,15 @@ static pax_status_t launch_tc_impl(const Problem& pr, cudaStream_t stream) {
     p.tiles_n = (int)((pr.N + BN - 1) / BN);
     p.num_tiles = p.tiles_m * p.tiles_n;
     p.group_m = PAIR ? 8 : 16;
+    p.full_items = plan.full_items;
+    p.split_tiles = plan.split_tiles;
+    p.num_items = plan.full_items + 2 * plan.split_tiles;
+    p.ws = ws;
+    p.counters = counters;
     p.epi = pr.epi;
+    if (p.num_tiles != plan.full_items + plan.split_tiles || (plan.split_tiles > 0 && (!ws || !counters)))
+        return PAX_ERR_INVALID;
 
-    const int dev = current_device();
-    const int sms = device_sm_count(dev);
     auto kern = gemm_tc_kernel<BN, STAGES, OutT, RES, GELU, PAIR>;
     // Attribute is per device; setting it again is cheap and idempotent.
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES) != cudaSuccess)
@@ -448,23 +539,43 @@ static pax_status_t launch_tc_impl(const Problem& pr, cudaStream_t stream) {
         cfg.stream = stream;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        cfg.gridDim = dim3(2 * 74);
-        // Pairs that can be resident at once (SMs pair up within a GPC).
-        static int max_pairs[64] = {0};
-        int& mp = max_pairs[dev & 63];
-        if (mp == 0) {
-            int n = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = sms / 2;
-            mp = n;
-        }
-        const int pairs = p.num_tiles < mp ? p.num_tiles : mp;
-        cfg.gridDim = dim3(2 * pairs);
+        cfg.gridDim = dim3(2 * plan.units);
         if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p) != cudaSuccess) return PAX_ERR_CUDA;
     } else {
-        const int grid = p.num_tiles < sms ? p.num_tiles : sms;
-        kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(tA, tB, tC, p);
+        kern<<<plan.units, 192, Cfg::SMEM_BYTES, stream>>>(tA, tB, tC, p);
     }
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
+}
+
+// Resident CTA pairs of the pair kernel on device `dev` (SMs pair up within
+// a GPC, so this can be below SMs / 2).
+template <typename OutT>
+static int tc_pair_units_typed(int dev, int sms) {
+    static int cache[64] = {0};
+    int& v = cache[dev & 63];
+    if (v == 0) {
+        using Cfg = TcCfg<256, 6, OutT, true>;
+        auto kern = gemm_tc_kernel<256, 6, OutT, 0, 0, true>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES);
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.blockDim = dim3(192);
+        cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cfg.gridDim = dim3(sms & ~1);
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = sms / 2;
+        }
+        v = n;
+    }
+    return v;
 }
 
 constexpr int kStages256 = 4;
@@ -473,29 +584,31 @@ constexpr int kStagesPair = 6;
 
 // Residual type and GeLU form are compile-time parameters so that each
 // instantiation carries only the epilogue code it runs.
+// Residual type and GeLU form are compile-time parameters so that each
+// instantiation carries only the epilogue code it runs.
 template <int BN, int STAGES, typename OutT, int GELU, bool PAIR>
-static pax_status_t launch_tc_gelu(const Problem& p, cudaStream_t stream) {
-    if (!(p.epi.flags & EPI_RES)) return launch_tc_impl<BN, STAGES, OutT, 0, GELU, PAIR>(p, stream);
-    if (p.epi.flags & EPI_RES_F32) return launch_tc_impl<BN, STAGES, OutT, 2, GELU, PAIR>(p, stream);
-    return launch_tc_impl<BN, STAGES, OutT, 1, GELU, PAIR>(p, stream);
+static pax_status_t launch_tc_gelu(const Problem& p, const TcPlan& plan, float* ws, int* cnt, cudaStream_t stream) {
+    if (!(p.epi.flags & EPI_RES)) return launch_tc_impl<BN, STAGES, OutT, 0, GELU, PAIR>(p, plan, ws, cnt, stream);
+    if (p.epi.flags & EPI_RES_F32) return launch_tc_impl<BN, STAGES, OutT, 2, GELU, PAIR>(p, plan, ws, cnt, stream);
+    return launch_tc_impl<BN, STAGES, OutT, 1, GELU, PAIR>(p, plan, ws, cnt, stream);
 }
 
 template <int BN, int STAGES, typename OutT, bool PAIR>
-static pax_status_t launch_tc_res(const Problem& p, cudaStream_t stream) {
+static pax_status_t launch_tc_res(const Problem& p, const TcPlan& plan, float* ws, int* cnt, cudaStream_t stream) {
     // GeLU-tanh uses the hardware tanh when the result is rounded to fp16
     // anyway, and tanhf for fp32 results.
     if (p.epi.flags & EPI_GELU_TANH)
-        return launch_tc_gelu<BN, STAGES, OutT, sizeof(OutT) == 2 ? 3 : 1, PAIR>(p, stream);
-    if (p.epi.flags & EPI_GELU_ERF) return launch_tc_gelu<BN, STAGES, OutT, 2, PAIR>(p, stream);
-    return launch_tc_gelu<BN, STAGES, OutT, 0, PAIR>(p, stream);
+        return launch_tc_gelu<BN, STAGES, OutT, sizeof(OutT) == 2 ? 3 : 1, PAIR>(p, plan, ws, cnt, stream);
+    if (p.epi.flags & EPI_GELU_ERF) return launch_tc_gelu<BN, STAGES, OutT, 2, PAIR>(p, plan, ws, cnt, stream);
+    return launch_tc_gelu<BN, STAGES, OutT, 0, PAIR>(p, plan, ws, cnt, stream);
 }
 
-// shape: 128 / 256 = one CTA per 128 x shape tile; 2 = CTA pair, 256 x 256 tile.
+// plan.shape: 128 / 256 = one CTA per 128 x shape tile; 2 = CTA pair, 256 x 256 tile.
 template <typename OutT>
-static pax_status_t launch_tc_typed(const Problem& p, int shape, cudaStream_t stream) {
-    if (shape == 2) return launch_tc_res<256, kStagesPair, OutT, true>(p, stream);
-    if (shape == 256) return launch_tc_res<256, kStages256, OutT, false>(p, stream);
-    return launch_tc_res<128, kStages128, OutT, false>(p, stream);
+static pax_status_t launch_tc_typed(const Problem& p, const TcPlan& plan, float* ws, int* cnt, cudaStream_t stream) {
+    if (plan.shape == 2) return launch_tc_res<256, kStagesPair, OutT, true>(p, plan, ws, cnt, stream);
+    if (plan.shape == 256) return launch_tc_res<256, kStages256, OutT, false>(p, plan, ws, cnt, stream);
+    return launch_tc_res<128, kStages128, OutT, false>(p, plan, ws, cnt, stream);
 }
 
 static int read_clear_device_error_this_unit() {

@@ -3,9 +3,11 @@
 
 namespace pax {
 
-pax_status_t launch_tc_f16(const Problem& p, int shape, cudaStream_t stream) {
-    return launch_tc_typed<__half>(p, shape, stream);
+pax_status_t launch_tc_f16(const Problem& p, const TcPlan& plan, float* ws, int* counters, cudaStream_t stream) {
+    return launch_tc_typed<__half>(p, plan, ws, counters, stream);
 }
+
+int tc_pair_units_f16(int dev, int sms) { return tc_pair_units_typed<__half>(dev, sms); }
 
 int read_clear_device_error_tc_f16() { return read_clear_device_error_this_unit(); }
 

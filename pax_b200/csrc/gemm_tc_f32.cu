@@ -3,9 +3,11 @@
 
 namespace pax {
 
-pax_status_t launch_tc_f32(const Problem& p, int shape, cudaStream_t stream) {
-    return launch_tc_typed<float>(p, shape, stream);
+pax_status_t launch_tc_f32(const Problem& p, const TcPlan& plan, float* ws, int* counters, cudaStream_t stream) {
+    return launch_tc_typed<float>(p, plan, ws, counters, stream);
 }
+
+int tc_pair_units_f32(int dev, int sms) { return tc_pair_units_typed<float>(dev, sms); }
 
 int read_clear_device_error_tc_f32() { return read_clear_device_error_this_unit(); }
 

@@ -164,6 +164,21 @@ __device__ __forceinline__ void cluster_sync() {
         "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// AND of `pred` over the `nthreads` threads that meet at named barrier `id`.
+template <int id, int nthreads>
+__device__ __forceinline__ bool named_barrier_and(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(pred ? 1u : 0u), "n"(id), "n"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
 // ----------------------------------------------------------------- tcgen05
 template <int kGroup>
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {

@@ -339,3 +339,32 @@ def test_deterministic(cuda, rng, algo, M):
 
 def test_no_device_errors_recorded(cuda):
     assert pax_b200.device_error() == pax_b200.Status.OK
+
+
+@pytest.mark.parametrize("shape,algo", [((4096, 4096, 512), "tc2"), ((4096, 4096, 512), "tc"), ((1024, 1024, 1024), "tc"),
+                                        ((1024, 1024, 1024), "tc2"), ((2304, 1280, 200), "tc2"), ((300, 520, 136), "tc")])
+@pytest.mark.parametrize("epi", ["bias_gelu_tanh", "residual_gelu_erf"])
+def test_tail_wave_split(cuda, rng, monkeypatch, shape, algo, epi):
+    """Tiles of the tail wave are split in two K halves joined through the
+    workspace (PAX_TC_SPLIT=1); shapes here leave a partial last wave (and odd
+    k-block counts)."""
+    monkeypatch.setenv("PAX_TC_SPLIT", "1")
+    M, N, K = shape
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    res = rng.standard_normal((M, N)).astype(np.float16)
+    for out in (np.float16, np.float32):
+        got = run_gemm(A, B, cuda, epi=epi, bias=bias, residual=res, out_dtype=out, algo=algo)
+        check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
+
+
+@pytest.mark.parametrize("algo", ["tc", "tc2"])
+def test_tail_wave_split_bit_exact_and_deterministic(cuda, rng, monkeypatch, algo):
+    monkeypatch.setenv("PAX_TC_SPLIT", "1")
+    A = rng.integers(-3, 4, (1024, 1024)).astype(np.float16)
+    B = rng.integers(-3, 4, (1024, 1024)).astype(np.float16)
+    exact = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.float32)
+    first = run_gemm(A, B, cuda, out_dtype=np.float32, algo=algo)
+    assert np.array_equal(first, exact)
+    for _ in range(3):
+        assert np.array_equal(run_gemm(A, B, cuda, out_dtype=np.float32, algo=algo), first)
