@@ -28,11 +28,12 @@ namespace pax {
 
 struct SkinnyParams {
     int M, N, K;
-    int num_tiles;  // ceil(N / 128)
+    int num_tiles;  // ceil(N / NT)
     int kblocks;    // ceil(K / 64)
     long long work; // num_tiles * kblocks
     int grid;       // number of CTAs (<= work)
-    float* ws;      // [grid][2][MP][128] fp32 partial sums
+    int slices;     // lockstep layout: K slices per tile (CTA = tile * slices + slice); 0 = stream-K
+    float* ws;      // [grid][2][MP][NT] fp32 partial sums
     int* counters;  // [num_tiles], zero between launches
     __half* c16;    // exactly one of c16 / c32 is set
     float* c32;
@@ -40,20 +41,28 @@ struct SkinnyParams {
     EpiParams epi;
 };
 
-template <int MP_>
+// MP: M padded to a multiple of 16 (the MMA N).  NT: output columns per work
+// unit, NT/128 MMAs of M = 128 per k-step.  Wider units make each k-row of B
+// a longer contiguous DRAM burst (NT * 2 bytes).
+template <int MP_, int NT_>
 struct SkCfg {
-    static constexpr int MP = MP_, BK = 64, TN = 128;
-    static constexpr uint32_t B_BYTES = TN * BK * 2;   // 16 KiB: two 64n x 64k boxes
+    static constexpr int MP = MP_, NT = NT_, BK = 64;
+    static constexpr int NSUB = NT / 128;
+    static constexpr uint32_t B_BYTES = NT * BK * 2;   // NT/64 boxes of 64n x 64k
     static constexpr uint32_t A_BYTES = MP * BK * 2;   // MP rows of 128 bytes
     static constexpr uint32_t STAGE_BYTES = B_BYTES + A_BYTES;
-    static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
-    static constexpr uint32_t TMEM_COLS = (2 * MP <= 32) ? 32 : (2 * MP <= 64) ? 64 : 128;
+    static constexpr int STAGES = (225 * 1024) / STAGE_BYTES;
+    static constexpr uint32_t ACC_COLS = NSUB * MP;  // one accumulator: NSUB blocks of MP columns
+    static constexpr uint32_t TMEM_COLS =
+        (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64 : (2 * ACC_COLS <= 128) ? 128 : (2 * ACC_COLS <= 256) ? 256 : 512;
     static constexpr uint32_t ACC_STRIDE = TMEM_COLS / 2;  // column offset of accumulator 1
     static constexpr uint32_t NUM_BARS = 2 * STAGES + 5;
     static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + NUM_BARS * 8 + 16;
     static constexpr uint32_t IDESC = umma_idesc_f16(128, MP, /*a_mn*/ true, /*b_mn*/ false);
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+    static_assert(STAGES >= 3, "at least three stages in flight");
     static_assert(A_BYTES % 1024 == 0, "A slot must keep 1024-byte swizzle alignment");
+    static_assert(2 * ACC_COLS <= 512, "two accumulators must fit in TMEM");
 };
 
 __device__ __forceinline__ long long sk_unit_begin(long long c, const SkinnyParams& p) {
@@ -64,12 +73,50 @@ __device__ __forceinline__ int sk_owner(long long x, const SkinnyParams& p) {
     return (int)(((x + 1) * p.grid + p.work - 1) / p.work - 1);
 }
 
-template <int MP>
+// One accumulation segment of a CTA: nk k-blocks kb0, kb0 + kstep, ... of
+// column tile `tile`.
+struct SkSeg {
+    int tile, kb0, kstep, nk;
+};
+
+// Segments of this CTA in order; `cursor` starts at sk_cursor0().
+//   stream-K: the CTA's contiguous unit range [ub, ue), cut at tile edges.
+//   lockstep: one segment, slice s = blockIdx.x % slices of tile
+//             blockIdx.x / slices takes k-blocks s, s + slices, ..., so all
+//             CTAs advance through the same k-rows of B together.
+__device__ __forceinline__ long long sk_cursor0(const SkinnyParams& p) {
+    return p.slices > 0 ? 0 : sk_unit_begin(blockIdx.x, p);
+}
+__device__ __forceinline__ bool sk_next_seg(const SkinnyParams& p, long long& cursor, SkSeg& sg) {
+    const int KB = p.kblocks;
+    if (p.slices > 0) {
+        if (cursor != 0) return false;
+        cursor = 1;
+        const int sl = (int)blockIdx.x % p.slices;
+        sg.tile = (int)blockIdx.x / p.slices;
+        sg.kb0 = sl;
+        sg.kstep = p.slices;
+        sg.nk = sl < KB ? (KB - sl + p.slices - 1) / p.slices : 0;
+        return sg.nk > 0;
+    }
+    const long long ue = sk_unit_begin(blockIdx.x + 1, p);
+    if (cursor >= ue) return false;
+    sg.tile = (int)(cursor / KB);
+    const long long seg_end = min(ue, (long long)(sg.tile + 1) * KB);
+    sg.kb0 = (int)(cursor - (long long)sg.tile * KB);
+    sg.kstep = 1;
+    sg.nk = (int)(seg_end - cursor);
+    cursor = seg_end;
+    return true;
+}
+
+template <int MP, int NT>
 __global__ void __launch_bounds__(192, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const SkinnyParams p) {
-    using Cfg = SkCfg<MP>;
+    using Cfg = SkCfg<MP, NT>;
     constexpr int STAGES = Cfg::STAGES;
+    constexpr int NSUB = Cfg::NSUB;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem =
         reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -89,8 +136,6 @@ __global__ void __launch_bounds__(192, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const long long ub = sk_unit_begin(blockIdx.x, p);
-    const long long ue = sk_unit_begin(blockIdx.x + 1, p);
     const int KB = p.kblocks;
 
     if (threadIdx.x == 0) {
@@ -125,9 +170,12 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t phase = 0;
             uint32_t issued = 0, last_parity = 0;
             bool ok = true;
-            for (long long u = ub; u < ue; ++u) {
-                const int tile = (int)(u / KB);
-                const int kb = (int)(u - (long long)tile * KB);
+            long long cur = sk_cursor0(p);
+            SkSeg sg;
+            while (ok && sk_next_seg(p, cur, sg))
+            for (int j = 0; j < sg.nk; ++j) {
+                const int tile = sg.tile;
+                const int kb = sg.kb0 + j * sg.kstep;
                 if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
                     ok = false;
                     break;
@@ -135,8 +183,10 @@ __global__ void __launch_bounds__(192, 1)
                 const uint32_t fb = full0 + 8u * stage;
                 mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
                 const uint32_t bdst = smem_u32(sB + stage * Cfg::B_BYTES);
-                tma_load_2d(bdst, &tmB, fb, tile * 128, kb * 64);
-                tma_load_2d(bdst + 8192u, &tmB, fb, tile * 128 + 64, kb * 64);
+                // All NT/64 boxes of this k-block together: NT*2 contiguous
+                // bytes of every k-row of B.
+#pragma unroll
+                for (int j = 0; j < NT / 64; ++j) tma_load_2d(bdst + j * 8192u, &tmB, fb, tile * NT + j * 64, kb * 64);
                 tma_load_2d(smem_u32(sA + stage * Cfg::A_BYTES), &tmA, fb, kb * 64, 0);
                 issued |= 1u << stage;
                 last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
@@ -156,26 +206,31 @@ __global__ void __launch_bounds__(192, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            long long u = ub;
-            while (ok && u < ue) {
-                const int tile = (int)(u / KB);
-                const long long seg_end = min(ue, (long long)(tile + 1) * KB);
+            long long cur = sk_cursor0(p);
+            SkSeg sg;
+            const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB), 8192, 1024);  // B^T, N-major
+            const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA), 16, 1024);    // A, K-major
+            while (ok && sk_next_seg(p, cur, sg)) {
                 if (!mbar_wait(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)acc * Cfg::ACC_STRIDE;
-                for (long long v = u; v < seg_end; ++v) {
+                for (int v = 0; v < sg.nk; ++v) {
                     if (!mbar_wait(full0 + 8u * stage, phase, abort_flag)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t b0 = smem_u32(sB + stage * Cfg::B_BYTES);
-                    const uint32_t a0 = smem_u32(sA + stage * Cfg::A_BYTES);
+                    const uint64_t bs = bdesc0 + (uint64_t)((stage * Cfg::B_BYTES) >> 4);
+                    const uint64_t as = adesc0 + (uint64_t)((stage * Cfg::A_BYTES) >> 4);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t ad = umma_desc_sw128(b0 + kk * 2048, 8192, 1024);  // B^T, N-major
-                        const uint64_t bd = umma_desc_sw128(a0 + kk * 32, 16, 1024);      // A, K-major
-                        tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (v != u || kk != 0) ? 1u : 0u);
+#pragma unroll
+                        for (int sb = 0; sb < NSUB; ++sb) {
+                            const uint64_t ad = bs + (uint64_t)((sb * 16384 + kk * 2048) >> 4);
+                            const uint64_t bd = as + (uint64_t)((kk * 32) >> 4);
+                            tc_mma_f16(d_tmem + (uint32_t)(sb * MP), ad, bd, Cfg::IDESC,
+                                       (v != 0 || kk != 0) ? 1u : 0u);
+                        }
                     }
                     tc_commit(empty0 + 8u * stage);
                     if (++stage == STAGES) {
@@ -189,7 +244,6 @@ __global__ void __launch_bounds__(192, 1)
                     acc = 0;
                     acc_phase ^= 1u;
                 }
-                u = seg_end;
             }
             tc_commit(drain_bar);
             mbar_wait(drain_bar, 0, nullptr);
@@ -198,33 +252,24 @@ __global__ void __launch_bounds__(192, 1)
         const int q = warp & 3;
         const int et = threadIdx.x - 64;  // 0..127 among epilogue threads
         const int n_local = q * 32 + lane;
-        const int first_tile = (int)(ub / KB);
+        const int first_tile = p.slices > 0 ? 0 : (int)(sk_unit_begin(blockIdx.x, p) / KB);
         int acc = 0;
         uint32_t acc_phase = 0;
-        long long u = ub;
-        while (u < ue) {
-            const int tile = (int)(u / KB);
-            const long long seg_begin = u;
-            const long long seg_end = min(ue, (long long)(tile + 1) * KB);
-            u = seg_end;
+        long long cur = sk_cursor0(p);
+        SkSeg sg;
+        while (sk_next_seg(p, cur, sg)) {
+            const int tile = sg.tile;
             // All four epilogue warps take the same branch (they meet at named
             // barriers below), so the wait outcome is AND-reduced across them.
-            const uint32_t ok_local = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag) ? 1u : 0u;
-            uint32_t ok_all;
-            asm volatile(
-                "{\n\t.reg .pred p, q;\n\t"
-                "setp.ne.u32 p, %1, 0;\n\t"
-                "bar.red.and.pred q, 1, 128, p;\n\t"
-                "selp.u32 %0, 1, 0, q;\n\t}"
-                : "=r"(ok_all)
-                : "r"(ok_local)
-                : "memory");
-            if (!ok_all) break;
+            const bool ok = named_barrier_and<1, 128>(mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag));
+            if (!ok) break;
             tc_fence_after();
-            float v[MP];
+            float v[NSUB][MP];
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)acc * Cfg::ACC_STRIDE;
 #pragma unroll
-            for (int j = 0; j < MP / 16; ++j) tmem_ld_32x32b_x16(t_row + 16u * j, v + 16 * j);
+            for (int sb = 0; sb < NSUB; ++sb)
+#pragma unroll
+                for (int j = 0; j < MP / 16; ++j) tmem_ld_32x32b_x16(t_row + (uint32_t)(sb * MP + 16 * j), v[sb] + 16 * j);
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
@@ -234,20 +279,29 @@ __global__ void __launch_bounds__(192, 1)
                 acc_phase ^= 1u;
             }
 
-            const long long n = (long long)tile * 128 + n_local;
-            const bool whole = (seg_begin == (long long)tile * KB) && (seg_end == (long long)(tile + 1) * KB);
+            const bool whole = p.slices > 0 ? p.slices == 1 : (sg.kb0 == 0 && sg.nk == KB);
             bool do_out = whole;
             if (!whole) {
                 // Park the partial sum, then count contributions for this tile.
-                const int slot = (tile == first_tile) ? 0 : 1;
-                float* wp = p.ws + ((size_t)blockIdx.x * 2 + slot) * (size_t)(MP * 128);
+                // Contributors: CTAs c_first..c_last; CTA c's partial for this
+                // tile is in its slot cslot(c).
+                const int slot = (p.slices > 0 || tile == first_tile) ? 0 : 1;
+                int c_first, c_last;
+                if (p.slices > 0) {
+                    c_first = tile * p.slices;
+                    c_last = c_first + min(p.slices, KB) - 1;
+                } else {
+                    c_first = sk_owner((long long)tile * KB, p);
+                    c_last = sk_owner((long long)(tile + 1) * KB - 1, p);
+                }
+                float* wp = p.ws + ((size_t)blockIdx.x * 2 + slot) * (size_t)(MP * NT);
 #pragma unroll
-                for (int m = 0; m < MP; ++m) wp[m * 128 + n_local] = v[m];
+                for (int sb = 0; sb < NSUB; ++sb)
+#pragma unroll
+                    for (int m = 0; m < MP; ++m) wp[m * NT + sb * 128 + n_local] = v[sb][m];
                 __threadfence();
                 asm volatile("bar.sync 1, 128;" ::: "memory");
                 if (et == 0) {
-                    const int c_first = sk_owner((long long)tile * KB, p);
-                    const int c_last = sk_owner((long long)(tile + 1) * KB - 1, p);
                     const int prev = atomicAdd(p.counters + tile, 1);
                     const int is_last = (prev == c_last - c_first) ? 1 : 0;
                     if (is_last) p.counters[tile] = 0;  // ready for the next launch
@@ -259,35 +313,43 @@ __global__ void __launch_bounds__(192, 1)
                 asm volatile("bar.sync 1, 128;" ::: "memory");
                 if (do_out) {
                     __threadfence();
-                    const int c_first = sk_owner((long long)tile * KB, p);
-                    const int c_last = sk_owner((long long)(tile + 1) * KB - 1, p);
 #pragma unroll
-                    for (int m = 0; m < MP; ++m) v[m] = 0.f;
+                    for (int sb = 0; sb < NSUB; ++sb)
+#pragma unroll
+                        for (int m = 0; m < MP; ++m) v[sb][m] = 0.f;
                     for (int c = c_first; c <= c_last; ++c) {
-                        const int cs = ((int)(sk_unit_begin(c, p) / KB) == tile) ? 0 : 1;
-                        const float* rp = p.ws + ((size_t)c * 2 + cs) * (size_t)(MP * 128);
+                        const int cs = (p.slices > 0 || (int)(sk_unit_begin(c, p) / KB) == tile) ? 0 : 1;
+                        const float* rp = p.ws + ((size_t)c * 2 + cs) * (size_t)(MP * NT);
 #pragma unroll
-                        for (int m = 0; m < MP; ++m) v[m] += __ldcg(rp + m * 128 + n_local);
+                        for (int sb = 0; sb < NSUB; ++sb)
+#pragma unroll
+                            for (int m = 0; m < MP; ++m) v[sb][m] += __ldcg(rp + m * NT + sb * 128 + n_local);
                     }
                 }
             }
-            if (do_out && n < p.N) {
+            if (do_out) {
                 const int flags = p.epi.flags;
-                const float b = (flags & EPI_BIAS) ? __half2float(p.epi.bias[n]) : 0.f;
 #pragma unroll
-                for (int m = 0; m < MP; ++m) {
-                    if (m < p.M) {
-                        float r = 0.f;
-                        if (flags & EPI_RES) {
-                            const long long off = (long long)m * p.epi.ld_res + n;
-                            r = (flags & EPI_RES_F32) ? static_cast<const float*>(p.epi.residual)[off]
-                                                      : __half2float(static_cast<const __half*>(p.epi.residual)[off]);
+                for (int sb = 0; sb < NSUB; ++sb) {
+                    const long long n = (long long)tile * NT + sb * 128 + n_local;
+                    if (n >= p.N) continue;
+                    const float b = (flags & EPI_BIAS) ? __half2float(p.epi.bias[n]) : 0.f;
+#pragma unroll
+                    for (int m = 0; m < MP; ++m) {
+                        if (m < p.M) {
+                            float r = 0.f;
+                            if (flags & EPI_RES) {
+                                const long long off = (long long)m * p.epi.ld_res + n;
+                                r = (flags & EPI_RES_F32)
+                                        ? static_cast<const float*>(p.epi.residual)[off]
+                                        : __half2float(static_cast<const __half*>(p.epi.residual)[off]);
+                            }
+                            const float o = epi_scalar(v[sb][m], b, r, flags, p.epi.alpha);
+                            if (p.c16)
+                                p.c16[(long long)m * p.ldc + n] = __float2half_rn(o);
+                            else
+                                p.c32[(long long)m * p.ldc + n] = o;
                         }
-                        const float o = epi_scalar(v[m], b, r, flags, p.epi.alpha);
-                        if (p.c16)
-                            p.c16[(long long)m * p.ldc + n] = __float2half_rn(o);
-                        else
-                            p.c32[(long long)m * p.ldc + n] = o;
                     }
                 }
             }
@@ -336,22 +398,46 @@ static bool sk_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
 
 int skinny_mp(long long M) { return (int)((M + 15) / 16) * 16; }
 
-void skinny_geometry(long long M, long long N, long long K, int sms, int* grid, size_t* ws_bytes,
-                     size_t* counter_bytes) {
+int skinny_pick_nt(long long M, long long N, long long K, int sms) {
+    const long long kb = (K + 63) / 64;
+    (void)M;
+    // 256-column units when every SM still gets at least four units to
+    // balance; the lockstep layout below always uses 128.
+    if (((N + 255) / 256) * kb >= 4LL * sms) return 256;
+    return 128;
+}
+
+// Lockstep layout: one CTA per (128-column tile, K slice), at most one CTA
+// per SM, slices interleaved by k-block.  Every SM then streams the same
+// number of bytes of B, the same k-rows at the same time, and a tile is
+// split only when there are SMs to spare for it.  Returns the number of K
+// slices (floor(SMs / tiles), at least 1), or 0 when there are more tiles
+// than SMs (persistent stream-K balances those better).
+int skinny_lockstep_slices(long long N, long long K, int sms) {
     const long long tiles = (N + 127) / 128;
+    const long long kb = (K + 63) / 64;
+    if (tiles > sms) return 0;
+    long long s = sms / tiles;
+    if (s > kb) s = kb;
+    return (int)(s < 1 ? 1 : s);
+}
+
+void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int* grid, size_t* ws_bytes,
+                     size_t* counter_bytes) {
+    const long long tiles = (N + nt - 1) / nt;
     const long long work = tiles * ((K + 63) / 64);
     long long g = sms;
     if (g > work) g = work;
     if (g < 1) g = 1;
     *grid = (int)g;
-    *ws_bytes = (size_t)g * 2 * (size_t)skinny_mp(M) * 128 * sizeof(float);
+    *ws_bytes = (size_t)g * 2 * (size_t)skinny_mp(M) * (size_t)nt * sizeof(float);
     *counter_bytes = (size_t)tiles * sizeof(int);
 }
 
-template <int MP>
-static pax_status_t launch_skinny_impl(const Problem& pr, int grid, float* ws, int* counters,
+template <int MP, int NT>
+static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, float* ws, int* counters,
                                        cudaStream_t stream) {
-    using Cfg = SkCfg<MP>;
+    using Cfg = SkCfg<MP, NT>;
     CUtensorMap tA, tB;
     if (!sk_tmap(&tA, pr.A, pr.K, pr.M, pr.lda * 2, 64, MP)) return PAX_ERR_CUDA;
     if (!sk_tmap(&tB, pr.B, pr.N, pr.K, pr.ldb * 2, 64, 64)) return PAX_ERR_CUDA;
@@ -359,31 +445,45 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, float* ws, i
     p.M = (int)pr.M;
     p.N = (int)pr.N;
     p.K = (int)pr.K;
-    p.num_tiles = (int)((pr.N + 127) / 128);
+    p.num_tiles = (int)((pr.N + NT - 1) / NT);
     p.kblocks = (int)((pr.K + 63) / 64);
     p.work = (long long)p.num_tiles * p.kblocks;
     p.grid = grid;
+    p.slices = slices;
     p.ws = ws;
     p.counters = counters;
     p.c16 = pr.c_f16 ? static_cast<__half*>(pr.C) : nullptr;
     p.c32 = pr.c_f16 ? nullptr : static_cast<float*>(pr.C);
     p.ldc = pr.ldc;
     p.epi = pr.epi;
-    auto kern = gemm_skinny_kernel<MP>;
+    if (grid < 1 || grid > p.work) return PAX_ERR_INVALID;
+    if (slices > 0 && slices * p.num_tiles != grid) return PAX_ERR_INVALID;
+    auto kern = gemm_skinny_kernel<MP, NT>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES) != cudaSuccess)
         return PAX_ERR_CUDA;
     kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(tA, tB, p);
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }
 
-pax_status_t launch_skinny_ws(const Problem& p, int grid, float* ws, int* counters, cudaStream_t stream) {
-    if (p.M < 1 || p.M > kSkinnyMaxM || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
+template <int NT>
+static pax_status_t launch_skinny_nt(const Problem& p, int grid, int slices, float* ws, int* counters,
+                                     cudaStream_t stream) {
     switch (skinny_mp(p.M)) {
-        case 16: return launch_skinny_impl<16>(p, grid, ws, counters, stream);
-        case 32: return launch_skinny_impl<32>(p, grid, ws, counters, stream);
-        case 48: return launch_skinny_impl<48>(p, grid, ws, counters, stream);
-        default: return launch_skinny_impl<64>(p, grid, ws, counters, stream);
+        case 16: return launch_skinny_impl<16, NT>(p, grid, slices, ws, counters, stream);
+        case 32: return launch_skinny_impl<32, NT>(p, grid, slices, ws, counters, stream);
+        case 48: return launch_skinny_impl<48, NT>(p, grid, slices, ws, counters, stream);
+        default: return launch_skinny_impl<64, NT>(p, grid, slices, ws, counters, stream);
     }
+}
+
+// nt: 128 or 256 output columns per unit.  slices > 0: lockstep layout (nt
+// 128, grid = tiles x slices); 0: persistent stream-K over `grid` CTAs.
+pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, int* counters, cudaStream_t stream,
+                              int slices) {
+    if (p.M < 1 || p.M > kSkinnyMaxM || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
+    if (slices > 0) return launch_skinny_nt<128>(p, grid, slices, ws, counters, stream);
+    if (nt == 256) return launch_skinny_nt<256>(p, grid, 0, ws, counters, stream);
+    return launch_skinny_nt<128>(p, grid, 0, ws, counters, stream);
 }
 
 int read_clear_device_error_skinny() {
@@ -446,7 +546,7 @@ extern "C" pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cud
                              "pax_gemm_skinny_noalloc: needs 1 <= m <= 64, k >= 1 and 16-byte aligned rows");
     int grid;
     size_t ws_bytes, cnt_bytes;
-    skinny_geometry(p.M, p.N, p.K, sms, &grid, &ws_bytes, &cnt_bytes);
+    skinny_geometry(p.M, p.N, p.K, sms, 128, &grid, &ws_bytes, &cnt_bytes);
     const size_t cnt_pad = (cnt_bytes + 255) & ~size_t(255);
     if (cnt_pad + ws_bytes > kNoAllocScratchBytes) {
         char msg[160];
@@ -462,7 +562,7 @@ extern "C" pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cud
     // start at zero.
     if (cudaMemsetAsync(scratch, 0, cnt_pad, stream) != cudaSuccess)
         return report_status(PAX_ERR_CUDA, "pax_gemm_skinny_noalloc: counter reset failed");
-    st = launch_skinny_ws(p, grid, reinterpret_cast<float*>(static_cast<char*>(scratch) + cnt_pad),
+    st = launch_skinny_ws(p, 128, grid, reinterpret_cast<float*>(static_cast<char*>(scratch) + cnt_pad),
                           static_cast<int*>(scratch), stream);
     if (st != PAX_OK) return report_status(st, "pax_gemm_skinny_noalloc: launch failed");
     return report_status(PAX_OK, "");

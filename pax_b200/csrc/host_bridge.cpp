@@ -258,15 +258,28 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
             if (!tma_compatible(p) || p.M > kSkinnyMaxM)
                 return fail(PAX_ERR_UNSUPPORTED, "skinny path needs m <= %lld and 16-byte aligned rows",
                             kSkinnyMaxM);
+            // Lockstep layout when there are no more column tiles than SMs;
+            // otherwise persistent stream-K, one CTA per SM.
+            // PAX_SKINNY_NT=128|256 forces the persistent layout.
+            int nt = env_int("PAX_SKINNY_NT", 0);
+            const int slices = (nt == 0) ? skinny_lockstep_slices(p.N, p.K, di.sms) : 0;
+            const bool lockstep = slices > 0;
+            if (lockstep) nt = 128;
+            if (nt != 128 && nt != 256) nt = skinny_pick_nt(p.M, p.N, p.K, di.sms);
             int grid;
             size_t ws_bytes, cnt_bytes;
-            skinny_geometry(p.M, p.N, p.K, di.sms, &grid, &ws_bytes, &cnt_bytes);
+            skinny_geometry(p.M, p.N, p.K, di.sms, nt, &grid, &ws_bytes, &cnt_bytes);
+            if (lockstep) {
+                const size_t per_cta = ws_bytes / (size_t)grid;
+                grid = (int)(((p.N + 127) / 128) * slices);
+                ws_bytes = per_cta * (size_t)grid;
+            }
             const size_t cnt_pad = (cnt_bytes + 255) & ~size_t(255);
             int* counters = nullptr;
             float* partials = nullptr;
             st = get_workspace(dev, s, cnt_pad, ws_bytes, &counters, &partials);
             if (st != PAX_OK) return fail(st, "skinny workspace allocation failed (%zu bytes)", cnt_pad + ws_bytes);
-            st = launch_skinny_ws(p, grid, partials, counters, s);
+            st = launch_skinny_ws(p, nt, grid, partials, counters, s, slices);
             break;
         }
         case PAX_ALGO_SIMT: st = launch_simt(p, s); break;

@@ -47,12 +47,19 @@ struct TcPlan {
 TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_split);
 pax_status_t launch_tc(const Problem& p, const TcPlan& plan, float* ws, int* counters, cudaStream_t stream);
 pax_status_t launch_simt(const Problem& p, cudaStream_t stream);
-// Skinny kernel: `ws` holds grid*2*MP*128 fp32 partial sums and `counters`
-// one int per 128-column tile, zero before the launch (the kernel leaves
-// them zero again).  skinny_geometry gives the grid and both sizes.
-void skinny_geometry(long long M, long long N, long long K, int sms, int* grid, size_t* ws_bytes,
+// Skinny kernel, nt (128, 256 or 512) output columns per work unit: `ws`
+// holds grid*2*MP*nt fp32 partial sums and `counters` one int per nt-column
+// tile, zero before the launch (the kernel leaves them zero again).
+// skinny_geometry gives the grid and both sizes; skinny_pick_nt the unit width.
+int skinny_pick_nt(long long M, long long N, long long K, int sms);
+int skinny_lockstep_slices(long long N, long long K, int sms);
+void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int* grid, size_t* ws_bytes,
                      size_t* counter_bytes);
-pax_status_t launch_skinny_ws(const Problem& p, int grid, float* ws, int* counters, cudaStream_t stream);
+// slices > 0 = the lockstep layout (nt 128, `grid` = tiles x slices CTAs,
+// one per SM); its workspace is sized by skinny_geometry with that grid's
+// per-CTA share.  slices = 0: persistent stream-K.
+pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, int* counters, cudaStream_t stream,
+                              int slices = 0);
 
 // Dynamic shared memory of the tcgen05 kernel for a tile shape / output type.
 size_t tc_smem_bytes(int shape, bool c_f16);

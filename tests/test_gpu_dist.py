@@ -1,0 +1,83 @@
+"""Column-slab GEMM on 2 GPUs (NCCL, one process per GPU): each rank runs the
+library kernel on its slab of B and C, the slabs are all-gathered, and the
+replicated C must match the oracle on every rank."""
+from __future__ import annotations
+
+import os
+import queue
+import socket
+import time
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, M, N, K, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import pax_b200
+    from pax_b200.dist import gather_columns, local_slab_gemm
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        g = torch.Generator().manual_seed(11)  # identical full inputs on every rank
+        A = (torch.rand((M, K), generator=g) * 2 - 1).half()
+        B = (torch.rand((K, N), generator=g) * 2 - 1).half()
+        bias = torch.randn((N,), generator=g).half()
+        C_slab = local_slab_gemm(A.to(dev), B.to(dev), rank, world, epilogue="bias_gelu_tanh", bias=bias.to(dev))
+        C = gather_columns(C_slab)
+        torch.cuda.synchronize()
+        q.put((rank, C.cpu().numpy(), int(pax_b200.device_error())))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_slabs_and_gather(cuda):
+    import oracle
+
+    world, M, N, K = 2, 512, 2048, 768
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    deadline = time.time() + 240
+    while len(got) < world and time.time() < deadline:
+        try:
+            r, C, err = q.get(timeout=1)
+            got[r] = (C, err)
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in procs):
+                break
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert len(got) == world, f"ranks failed: {[p.exitcode for p in procs]}"
+    g = torch.Generator().manual_seed(11)
+    A = (torch.rand((M, K), generator=g) * 2 - 1).half().numpy()
+    B = (torch.rand((K, N), generator=g) * 2 - 1).half().numpy()
+    bias = torch.randn((N,), generator=g).half().numpy()
+    ref = oracle.gemm(A, B, epi="bias_gelu_tanh", bias=bias, out_dtype=np.float16)
+    for r, (C, err) in got.items():
+        assert err == 0
+        assert oracle.normwise_error(C, ref) <= 2e-3
+    assert np.array_equal(got[0][0].view(np.uint16), got[1][0].view(np.uint16))

@@ -113,6 +113,20 @@ def test_skinny(cuda, rng, M, NK):
     check(got, oracle.gemm(A, B, epi="bias", bias=bias, out_dtype=np.float16), np.float16)
 
 
+@pytest.mark.parametrize("nt", [0, 128, 256])
+@pytest.mark.parametrize("M,N,K", [(16, 16384, 4096), (1, 1000, 320), (33, 2048, 1088), (64, 768, 4096),
+                                   (16, 520, 64), (16, 40960, 2048), (48, 16384, 4160)])
+def test_skinny_layouts(cuda, rng, monkeypatch, nt, M, N, K):
+    """Lockstep layout (nt=0: one CTA per (tile, interleaved K slice)) and the
+    persistent stream-K layout with 128- and 256-column units, including
+    ragged N, uneven K slices and tiles split between CTAs."""
+    monkeypatch.setenv("PAX_SKINNY_NT", str(nt))
+    A, B = inputs(rng, M, N, K, dist="normal")
+    bias = rng.standard_normal(N).astype(np.float16)
+    got = run_gemm(A, B, cuda, epi="bias", bias=bias, out_dtype=np.float16, algo="skinny")
+    check(got, oracle.gemm(A, B, epi="bias", bias=bias, out_dtype=np.float16), np.float16)
+
+
 @pytest.mark.parametrize("epi", ["none", "bias_gelu_erf", "residual_gelu_tanh"])
 @pytest.mark.parametrize("out", [np.float32, np.float16])
 def test_skinny_epilogues(cuda, rng, epi, out):
