@@ -14,7 +14,8 @@
 //     0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
 //   exact form (no reference code; the definition PAX/GEMM.lean:150-152
 //   bounds the tanh form against): 0.5 x (1 + erf(x / sqrt 2))
-// Both call CUDA's tanhf / erff.
+// tanh: CUDA's tanhf, or the hardware tanh.approx.f32 for fp16 results;
+// erf: CUDA's erff.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -48,6 +49,7 @@ __device__ __forceinline__ float gelu_tanh_hw(float x) {
 __device__ __forceinline__ float gelu_erf(float x) {
     return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
+
 
 // One output value: scale, then bias and/or residual, then GeLU.  `b` is the
 // bias value and `r` the residual value (ignored unless their flag is set).
@@ -150,7 +152,7 @@ __device__ __forceinline__ uint4 bias_tile_load(long long tile_col0, int tile_co
 // Epilogue of one row chunk of n columns starting at tile column `tc` (a
 // multiple of 8), in two phases so the caller can refill `rc` in between:
 //   epi_linear: v = alpha*v (+ bias[j]) (+ R[i][j])
-//   epi_gelu:   v = GeLU(v)     GELU: 0 none, 1 tanh (tanhf), 2 erf, 3 tanh (tanh.approx)
+//   epi_gelu:   v = GeLU(v)     GELU: 0 none, 1 tanh (tanhf), 2 erf (erff), 3 tanh (tanh.approx)
 // `bias8` is this lane's bias_tile_load value.
 template <int n, int RES>
 __device__ __forceinline__ void epi_linear(float (&v)[n], const ResChunk<n, RES>& rc, uint4 bias8, int tc,

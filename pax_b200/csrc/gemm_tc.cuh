@@ -31,6 +31,7 @@
 #include "epilogue.cuh"
 
 #include <cudaTypedefs.h>
+#include <stdlib.h>
 #include <mutex>
 #include <stdio.h>
 
@@ -315,8 +316,8 @@ __global__ void __launch_bounds__(192, 1)
             // Operands that do not depend on the accumulator are fetched before
             // waiting for it: this tile's bias and the first residual chunk.
             const uint4 bias8 = bias_tile_load(tcol0, BN, lane, p.N, p.epi);
-            ResChunk<EC, RES> rc;
-            res_prefetch<EC, RES>(rc, row, tcol0, p.M, p.N, p.epi);
+            ResChunk<32, RES> rc;
+            res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, p.epi);
             bool ok = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag);
             // Split items meet at named barriers below, so all four epilogue
             // warps must take the same branch.
@@ -382,31 +383,44 @@ __global__ void __launch_bounds__(192, 1)
                 other = p.ws + ((size_t)(2 * sidx + (part ^ 1)) * 128 + row_local) * BN;
             }
             if (nch == 0) release_accumulator();
+            // Each chunk is one 128-byte output row per lane (EC columns), built
+            // from 32-column sub-chunks: TMEM load, epilogue, GeLU, pack.  Only
+            // 32 fp32 values are live at a time.
 #pragma unroll 1
             for (int ci = 0; ci < nch; ++ci) {
-                const int c = ci * EC;
-                float v[EC];
-                tmem_ld_32x32b_x32(t_row + (uint32_t)c, v);
-                if constexpr (EC == 64) tmem_ld_32x32b_x32(t_row + (uint32_t)c + 32u, v + 32);
-                tmem_wait_ld();
-                if (ci == nch - 1) release_accumulator();
-                if (other != nullptr) {
+                uint32_t w[32];  // packed output row
 #pragma unroll
-                    for (int i = 0; i < EC; i += 4) {
-                        const float4 o = __ldcg(reinterpret_cast<const float4*>(other + c + i));
-                        v[i] += o.x;
-                        v[i + 1] += o.y;
-                        v[i + 2] += o.z;
-                        v[i + 3] += o.w;
+                for (int h = 0; h < EC / 32; ++h) {
+                    const int c = ci * EC + 32 * h;
+                    float v[32];
+                    tmem_ld_32x32b_x32(t_row + (uint32_t)c, v);
+                    tmem_wait_ld();
+                    if (ci == nch - 1 && h == EC / 32 - 1) release_accumulator();
+                    if (other != nullptr) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            const float4 o = __ldcg(reinterpret_cast<const float4*>(other + c + i));
+                            v[i] += o.x;
+                            v[i + 1] += o.y;
+                            v[i + 2] += o.z;
+                            v[i + 3] += o.w;
+                        }
+                    }
+                    epi_linear<32, RES>(v, rc, bias8, c, p.epi);
+                    // The residual registers are free again: start the next
+                    // sub-chunk's loads, which then overlap the GeLU math below.
+                    if constexpr (RES != 0) {
+                        if (c + 32 < nch * EC) res_prefetch<32, RES>(rc, row, tcol0 + c + 32, p.M, p.N, p.epi);
+                    }
+                    epi_gelu<32, GELU>(v);
+#pragma unroll
+                    for (int i = 0; i < 32 * (int)sizeof(OutT) / 4; ++i) {
+                        if constexpr (sizeof(OutT) == 2)
+                            w[16 * h + i] = pack_half2(v[2 * i], v[2 * i + 1]);
+                        else
+                            w[i] = __float_as_uint(v[i]);
                     }
                 }
-                epi_linear<EC, RES>(v, rc, bias8, c, p.epi);
-                // The residual registers are free again: start the next
-                // chunk's loads, which then overlap the GeLU math below.
-                if constexpr (RES != 0) {
-                    if (ci + 1 < nch) res_prefetch<EC, RES>(rc, row, tcol0 + c + EC, p.M, p.N, p.epi);
-                }
-                epi_gelu<EC, GELU>(v);
                 // Staging buffer (ci & 1) is free once at most one store group
                 // (the previous chunk's, using the other buffer) is still
                 // reading; every processed chunk commits exactly one group.
@@ -416,25 +430,14 @@ __global__ void __launch_bounds__(192, 1)
                 const uint32_t srow = smem_u32(sbuf) + (uint32_t)lane * 128u;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    uint32_t w0, w1, w2, w3;
-                    if constexpr (sizeof(OutT) == 2) {
-                        w0 = pack_half2(v[8 * j + 0], v[8 * j + 1]);
-                        w1 = pack_half2(v[8 * j + 2], v[8 * j + 3]);
-                        w2 = pack_half2(v[8 * j + 4], v[8 * j + 5]);
-                        w3 = pack_half2(v[8 * j + 6], v[8 * j + 7]);
-                    } else {
-                        w0 = __float_as_uint(v[4 * j + 0]);
-                        w1 = __float_as_uint(v[4 * j + 1]);
-                        w2 = __float_as_uint(v[4 * j + 2]);
-                        w3 = __float_as_uint(v[4 * j + 3]);
-                    }
                     // 128B swizzle: 16-byte chunk j of row r lives at chunk j ^ (r % 8).
-                    st_shared_v4(srow + (uint32_t)((j ^ (lane & 7)) << 4), w0, w1, w2, w3);
+                    st_shared_v4(srow + (uint32_t)((j ^ (lane & 7)) << 4), w[4 * j], w[4 * j + 1], w[4 * j + 2],
+                                 w[4 * j + 3]);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_2d(&tmC, smem_u32(sbuf), (int)(tcol0 + c), row0);
+                    tma_store_2d(&tmC, smem_u32(sbuf), (int)(tcol0 + ci * EC), row0);
                     bulk_commit();
                 }
             }
