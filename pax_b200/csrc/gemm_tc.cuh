@@ -8,14 +8,15 @@
 // src/rtx_gemm_epilogue.cu:243-356); the epilogue semantics are those of
 // src/rtx_gemm_epilogue.cu:176-233 (see epilogue.cuh).
 //
-// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
+// CTA layout (320 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A tile 128x64 (K-major) and B tile 64xBN
 //               (N-major) per k-block into a STAGES-deep ring of
 //               128B-swizzled shared-memory slots, mbarrier full/empty pairs.
 //   warp 1      MMA issuer: allocates TMEM (2 accumulators of 128 lanes x BN
 //               fp32 columns), issues tcgen05.mma M=128 N=BN K=16 (four per
 //               k-block), commits slot releases and accumulator-ready.
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x {32|64} columns, bias /
+//   warps 2..9  epilogue, two per TMEM lane quarter, each on half of the
+//               tile's columns: tcgen05.ld 32 lanes x 32 columns, bias /
 //               residual / GeLU in registers, fp32->fp16, swizzled staging
 //               in shared memory, TMA store.  Accumulator i is handed back to
 //               the MMA warp as soon as it is read, so the epilogue of tile t
@@ -86,8 +87,13 @@ struct TcCfg {
     static constexpr uint32_t B_BYTES = BN_LOCAL * BK * 2;  // 16 / 32 KiB
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_COLS = 128 / (int)sizeof(OutT);  // one 128-byte row per chunk
-    static constexpr uint32_t STG_BYTES = 32 * 128;            // per warp, per buffer
-    static constexpr uint32_t STG_TOTAL = 4 * 2 * STG_BYTES;
+    // Epilogue: two warps per TMEM lane quarter, each owning half of the
+    // tile's columns, one staging buffer each.
+    static constexpr int EPI_WARPS = 8;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int EPI_HALF_COLS = BN / 2;
+    static constexpr uint32_t STG_BYTES = 32 * 128;            // per warp
+    static constexpr uint32_t STG_TOTAL = EPI_WARPS * STG_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
     static constexpr uint32_t NUM_BARS = 2 * STAGES + 5;
     static constexpr size_t SMEM_BYTES =
@@ -109,7 +115,7 @@ __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& mb, i
 }
 
 template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(64 + 32 * 8, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const TcParams p) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
@@ -146,7 +152,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull0 + 8u * b, 1);
             // one arrive per epilogue warp (of both CTAs in pair mode)
-            mbar_init(tempty0 + 8u * b, PAIR ? 8 : 4);
+            mbar_init(tempty0 + 8u * b, PAIR ? 2 * Cfg::EPI_WARPS : Cfg::EPI_WARPS);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -300,8 +306,10 @@ __global__ void __launch_bounds__(192, 1)
     } else {
         // ------------------------------------------------ epilogue warps
         constexpr int EC = Cfg::EPI_COLS;
-        const int q = warp & 3;  // TMEM lane quarter this warp may read
-        uint8_t* stg = sStg + (warp - 2) * 2 * Cfg::STG_BYTES;
+        constexpr int HC = Cfg::EPI_HALF_COLS;
+        const int q = warp & 3;            // TMEM lane quarter this warp may read
+        const int hcol = ((warp - 2) >> 2) * HC;  // first tile column of this warp's half
+        uint8_t* sbuf = sStg + (warp - 2) * Cfg::STG_BYTES;
         int acc = 0;
         uint32_t acc_phase = 0;
         volatile int* last_flag = abort_flag + 1;
@@ -312,22 +320,22 @@ __global__ void __launch_bounds__(192, 1)
             tile_coords(t, p, mb, nb);
             const int row0 = mb * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
             const long long row = (long long)row0 + lane;
-            const long long tcol0 = (long long)nb * BN;
+            const long long tcol0 = (long long)nb * BN + hcol;  // this warp's first column
             // Operands that do not depend on the accumulator are fetched before
-            // waiting for it: this tile's bias and the first residual chunk.
-            const uint4 bias8 = bias_tile_load(tcol0, BN, lane, p.N, p.epi);
+            // waiting for it: this half tile's bias and the first residual chunk.
+            const uint4 bias8 = bias_tile_load(tcol0, HC, lane, p.N, p.epi);
             ResChunk<32, RES> rc;
             res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, p.epi);
             bool ok = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag);
             // Split items meet at named barriers below, so all four epilogue
             // warps must take the same branch.
-            ok = part >= 0 ? named_barrier_and<1, 128>(ok) : __all_sync(0xffffffffu, ok);
+            ok = part >= 0 ? named_barrier_and<1, 32 * Cfg::EPI_WARPS>(ok) : __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + hcol);
             // Chunks wholly outside C (beyond N, or this warp's 32 rows beyond
             // M) are neither read nor stored.
-            const long long valid_cols = p.N - tcol0 < BN ? p.N - tcol0 : BN;
+            const long long valid_cols = p.N - tcol0 < HC ? (p.N - tcol0 > 0 ? p.N - tcol0 : 0) : HC;
             const int nch = row0 < p.M ? (int)((valid_cols + EC - 1) / EC) : 0;
             auto release_accumulator = [&]() {
                 // Whole accumulator read: hand it back to the MMA warp (of the
@@ -348,7 +356,7 @@ __global__ void __launch_bounds__(192, 1)
             if (part >= 0) {
                 const int sidx = (t - p.full_items) * (PAIR ? 2 : 1) + (int)rank;
                 const int row_local = q * 32 + lane;
-                float* mine = p.ws + ((size_t)(2 * sidx + part) * 128 + row_local) * BN;
+                float* mine = p.ws + ((size_t)(2 * sidx + part) * 128 + row_local) * BN + hcol;
                 if (row0 < p.M) {
 #pragma unroll 1
                     for (int c = 0; c < (int)valid_cols; c += 32) {
@@ -361,16 +369,16 @@ __global__ void __launch_bounds__(192, 1)
                     }
                 }
                 __threadfence();
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                named_barrier_sync<1, 32 * Cfg::EPI_WARPS>();
                 if (warp == 2 && lane == 0) {
                     const int prev = atomicAdd(p.counters + sidx, 1);
                     const int is_last = prev == 1 ? 1 : 0;
                     if (is_last) p.counters[sidx] = 0;  // ready for the next launch
                     *last_flag = is_last;
                 }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                named_barrier_sync<1, 32 * Cfg::EPI_WARPS>();
                 const bool is_last = *last_flag != 0;
-                asm volatile("bar.sync 1, 128;" ::: "memory");  // flag read by all before reuse
+                named_barrier_sync<1, 32 * Cfg::EPI_WARPS>();  // flag read by all before reuse
                 if (!is_last) {
                     release_accumulator();
                     if (++acc == 2) {
@@ -380,7 +388,7 @@ __global__ void __launch_bounds__(192, 1)
                     continue;
                 }
                 __threadfence();
-                other = p.ws + ((size_t)(2 * sidx + (part ^ 1)) * 128 + row_local) * BN;
+                other = p.ws + ((size_t)(2 * sidx + (part ^ 1)) * 128 + row_local) * BN + hcol;
             }
             if (nch == 0) release_accumulator();
             // Each chunk is one 128-byte output row per lane (EC columns), built
@@ -421,12 +429,10 @@ __global__ void __launch_bounds__(192, 1)
                             w[i] = __float_as_uint(v[i]);
                     }
                 }
-                // Staging buffer (ci & 1) is free once at most one store group
-                // (the previous chunk's, using the other buffer) is still
-                // reading; every processed chunk commits exactly one group.
-                if (lane == 0) bulk_wait_read<1>();
+                // The staging buffer is free once this warp's previous store
+                // has finished reading it.
+                if (lane == 0) bulk_wait_read<0>();
                 __syncwarp();
-                uint8_t* sbuf = stg + (ci & 1) * Cfg::STG_BYTES;
                 const uint32_t srow = smem_u32(sbuf) + (uint32_t)lane * 128u;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
@@ -537,7 +543,7 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, float*
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
-        cfg.blockDim = dim3(192);
+        cfg.blockDim = dim3(Cfg::THREADS);
         cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
         cfg.stream = stream;
         cfg.attrs = attr;
@@ -545,7 +551,7 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, float*
         cfg.gridDim = dim3(2 * plan.units);
         if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p) != cudaSuccess) return PAX_ERR_CUDA;
     } else {
-        kern<<<plan.units, 192, Cfg::SMEM_BYTES, stream>>>(tA, tB, tC, p);
+        kern<<<plan.units, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(tA, tB, tC, p);
     }
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }
@@ -566,7 +572,7 @@ static int tc_pair_units_typed(int dev, int sms) {
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
-        cfg.blockDim = dim3(192);
+        cfg.blockDim = dim3(Cfg::THREADS);
         cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
         cfg.attrs = attr;
         cfg.numAttrs = 1;

@@ -164,6 +164,12 @@ __device__ __forceinline__ void cluster_sync() {
         "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// Named barrier `id` over `nthreads` threads.
+template <int id, int nthreads>
+__device__ __forceinline__ void named_barrier_sync() {
+    asm volatile("bar.sync %0, %1;" ::"n"(id), "n"(nthreads) : "memory");
+}
+
 // AND of `pred` over the `nthreads` threads that meet at named barrier `id`.
 template <int id, int nthreads>
 __device__ __forceinline__ bool named_barrier_and(bool pred) {
