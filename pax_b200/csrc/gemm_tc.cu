@@ -5,8 +5,8 @@
 
 namespace pax {
 
-pax_status_t launch_tc_f16(const Problem& p, const TcPlan& plan, float* ws, int* counters, cudaStream_t stream);
-pax_status_t launch_tc_f32(const Problem& p, const TcPlan& plan, float* ws, int* counters, cudaStream_t stream);
+pax_status_t launch_tc_f16(const Problem& p, const TcPlan& plan, cudaStream_t stream);
+pax_status_t launch_tc_f32(const Problem& p, const TcPlan& plan, cudaStream_t stream);
 int tc_pair_units_f16(int dev, int sms);
 int read_clear_device_error_tc_f16();
 int read_clear_device_error_tc_f32();
@@ -45,32 +45,28 @@ int tc_pick_shape(long long M, long long N, int sms) {
     return t256 <= t128 ? 256 : 128;
 }
 
-TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_split) {
+TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_halves) {
     TcPlan plan;
     plan.shape = (shape == 2 || shape == 256) ? shape : 128;
     const long long tile_m = plan.shape == 2 ? 256 : 128;
     const long long tile_n = plan.shape == 128 ? 128 : 256;
-    const long long bn = tile_n;
-    const long long ctas_per_tile = plan.shape == 2 ? 2 : 1;
     const long long tiles = ((p.M + tile_m - 1) / tile_m) * ((p.N + tile_n - 1) / tile_n);
     const long long max_units = plan.shape == 2 ? tc_pair_units_f16(dev, sms) : sms;
-    const long long num_kb = (p.K + 63) / 64;
     // The tail wave: tiles left after whole waves.  When at most half the
-    // units would be busy on them, each is split into two K halves.
+    // units would be busy on them, each is cut into two column halves, so
+    // the tail takes about half the time of a wave.
     const long long rem = tiles >= max_units ? tiles % max_units : tiles;
-    const bool split = allow_split && rem > 0 && 2 * rem <= max_units && num_kb >= 2;
-    plan.split_tiles = split ? (int)rem : 0;
-    plan.full_items = (int)(tiles - plan.split_tiles);
-    const long long items = plan.full_items + 2LL * plan.split_tiles;
+    const bool halves = allow_halves && rem > 0 && 2 * rem <= max_units;
+    plan.tail_tiles = halves ? (int)rem : 0;
+    plan.full_items = (int)(tiles - plan.tail_tiles);
+    const long long items = plan.full_items + 2LL * plan.tail_tiles;
     plan.units = (int)(items < max_units ? items : max_units);
-    plan.cnt_bytes = (size_t)plan.split_tiles * ctas_per_tile * sizeof(int);
-    plan.ws_bytes = (size_t)plan.split_tiles * 2 * ctas_per_tile * 128 * bn * sizeof(float);
     return plan;
 }
 
-pax_status_t launch_tc(const Problem& p, const TcPlan& plan, float* ws, int* counters, cudaStream_t stream) {
+pax_status_t launch_tc(const Problem& p, const TcPlan& plan, cudaStream_t stream) {
     if (p.M > 0x7fffffffLL || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
-    return p.c_f16 ? launch_tc_f16(p, plan, ws, counters, stream) : launch_tc_f32(p, plan, ws, counters, stream);
+    return p.c_f16 ? launch_tc_f16(p, plan, stream) : launch_tc_f32(p, plan, stream);
 }
 
 int read_clear_device_error_tc() {

@@ -42,31 +42,23 @@ struct TcParams {
     int M, N, K;
     int tiles_m, tiles_n, num_tiles;
     int group_m;  // output tiles are visited in column-major groups of group_m tile rows
-    // Work items: tiles [0, full_items) whole, then the last split_tiles
-    // tiles in two K halves each (the tail wave), so
-    // num_items = full_items + 2 * split_tiles.
-    int full_items, split_tiles, num_items;
-    float* ws;      // split partials: [split_tiles][2 halves][CTAs per tile][128][BN] fp32
-    int* counters;  // [split_tiles][CTAs per tile], zero between launches
+    // Work items: tiles [0, full_items) whole, then the last tail_tiles tiles
+    // (the tail wave) as two column halves each, so
+    // num_items = full_items + 2 * tail_tiles.
+    int full_items, tail_tiles, num_items;
     EpiParams epi;
 };
 
-// Work item -> output tile and k-block range [kb0, kb1); part = -1 for a
-// whole tile, else which K half of a split tile.
-__device__ __forceinline__ void tc_item(int item, const TcParams& p, int num_kb, int& tile, int& kb0, int& kb1,
-                                        int& part) {
+// Work item -> output tile and column half: half = -1 for a whole tile, else
+// 0 / 1 for the left / right BN/2 columns of a tail tile.
+__device__ __forceinline__ void tc_item(int item, const TcParams& p, int& tile, int& half) {
     if (item < p.full_items) {
         tile = item;
-        kb0 = 0;
-        kb1 = num_kb;
-        part = -1;
+        half = -1;
     } else {
         const int j = item - p.full_items;
         tile = p.full_items + (j >> 1);
-        part = j & 1;
-        const int h = num_kb >> 1;
-        kb0 = part ? h : 0;
-        kb1 = part ? num_kb : h;
+        half = j & 1;
     }
 }
 
@@ -74,7 +66,8 @@ __device__ __forceinline__ void tc_item(int item, const TcParams& p, int num_kb,
 // tcgen05.mma.cta_group::1.  PAIR = true: a cluster of two CTAs computes a
 // 256 x BN tile with tcgen05.mma.cta_group::2 issued by the even CTA; each
 // CTA stages its own 128 rows of A and BN/2 columns of B, and holds its 128
-// rows of the accumulator in its own TMEM.
+// rows of the accumulator in its own TMEM.  A column-half item is the same
+// with BN/2 accumulator columns (MMA N = BN/2).
 template <int BN_, int STAGES_, typename OutT, bool PAIR_>
 struct TcCfg {
     static constexpr bool PAIR = PAIR_;
@@ -88,10 +81,9 @@ struct TcCfg {
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_COLS = 128 / (int)sizeof(OutT);  // one 128-byte row per chunk
     // Epilogue: two warps per TMEM lane quarter, each owning half of the
-    // tile's columns, one staging buffer each.
+    // item's columns (at least one 128-byte chunk), one staging buffer each.
     static constexpr int EPI_WARPS = 8;
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-    static constexpr int EPI_HALF_COLS = BN / 2;
     static constexpr uint32_t STG_BYTES = 32 * 128;            // per warp
     static constexpr uint32_t STG_TOTAL = EPI_WARPS * STG_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -99,9 +91,10 @@ struct TcCfg {
     static constexpr size_t SMEM_BYTES =
         1024 + (size_t)STAGES * STAGE_BYTES + STG_TOTAL + NUM_BARS * 8 + 16;
     static constexpr uint32_t IDESC = umma_idesc_f16(PAIR ? 256 : 128, BN, /*a_mn*/ false, /*b_mn*/ true);
+    static constexpr uint32_t IDESC_HALF = umma_idesc_f16(PAIR ? 256 : 128, BN / 2, false, true);
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
-    static_assert(BN_LOCAL % 64 == 0, "B is staged in 64-column boxes");
+    static_assert((BN_LOCAL / 2) % 64 == 0, "B (and a half of it) is staged in 64-column boxes");
 };
 
 __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& mb, int& nb) {
@@ -185,13 +178,18 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             bool ok = true;
             uint32_t issued = 0, last_parity = 0;
             for (int item = unit; ok && item < p.num_items; item += units) {
-                int t, kb0, kb1, part;
-                tc_item(item, p, num_kb, t, kb0, kb1, part);
+                int t, half;
+                tc_item(item, p, t, half);
                 int mb, nb;
                 tile_coords(t, p, mb, nb);
+                // The item's columns start at ncol0; this CTA stages `wl` of
+                // them (its half of them in pair mode).
+                const int wl = half < 0 ? Cfg::BN_LOCAL : Cfg::BN_LOCAL / 2;
+                const int ncol0 = nb * BN + (half > 0 ? BN / 2 : 0);
                 const int arow = mb * Cfg::TILE_M + (int)rank * Cfg::BM;
-                const int bcol = nb * BN + (int)rank * Cfg::BN_LOCAL;
-                for (int kb = kb0; kb < kb1; ++kb) {
+                const int bcol = ncol0 + (int)rank * wl;
+                const uint32_t bytes = Cfg::A_BYTES + (uint32_t)wl * Cfg::BK * 2;
+                for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
                         ok = false;
                         break;
@@ -203,16 +201,14 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         // Both CTAs' loads complete on the leader's full barrier;
                         // the leader announces the bytes of both.
                         const uint32_t fb_leader = mapa_shared(fb, 0);
-                        if (leader) mbar_arrive_expect_tx(fb, 2 * Cfg::STAGE_BYTES);
+                        if (leader) mbar_arrive_expect_tx(fb, 2 * bytes);
                         tma_load_2d_pair(adst, &tmA, fb_leader, kb * Cfg::BK, arow);
-#pragma unroll
-                        for (int j = 0; j < Cfg::BN_LOCAL / 64; ++j)
+                        for (int j = 0; j < wl / 64; ++j)
                             tma_load_2d_pair(bdst + j * 8192, &tmB, fb_leader, bcol + j * 64, kb * Cfg::BK);
                     } else {
-                        mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+                        mbar_arrive_expect_tx(fb, bytes);
                         tma_load_2d(adst, &tmA, fb, kb * Cfg::BK, arow);
-#pragma unroll
-                        for (int j = 0; j < Cfg::BN_LOCAL / 64; ++j)
+                        for (int j = 0; j < wl / 64; ++j)
                             tma_load_2d(bdst + j * 8192, &tmB, fb, bcol + j * 64, kb * Cfg::BK);
                     }
                     issued |= 1u << stage;
@@ -249,13 +245,14 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA), 16, 1024);
             const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB), 8192, 1024);
             for (int item = unit; ok && item < p.num_items; item += units) {
-                int t, kb0, kb1, part;
-                tc_item(item, p, num_kb, t, kb0, kb1, part);
+                int t, half;
+                tc_item(item, p, t, half);
+                const uint32_t idesc = half < 0 ? Cfg::IDESC : Cfg::IDESC_HALF;
                 // In pair mode the releases come from both CTAs' epilogues.
                 if (!mbar_wait<PAIR>(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-                for (int kb = kb0; kb < kb1; ++kb) {
+                for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(full0 + 8u * stage, phase, abort_flag)) {
                         ok = false;
                         break;
@@ -268,9 +265,9 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         const uint64_t ad = as + (uint64_t)((kk * 32) >> 4);    // +32 B along K
                         const uint64_t bd = bs + (uint64_t)((kk * 2048) >> 4);  // +16 rows of K
                         if constexpr (PAIR)
-                            tc_mma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
+                            tc_mma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
                         else
-                            tc_mma_f16(d_tmem, ad, bd, Cfg::IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
+                            tc_mma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
                     }
                     if constexpr (PAIR) {
                         tc_commit_pair(mapa_shared(empty0 + 8u * stage, 0));
@@ -306,36 +303,41 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     } else {
         // ------------------------------------------------ epilogue warps
         constexpr int EC = Cfg::EPI_COLS;
-        constexpr int HC = Cfg::EPI_HALF_COLS;
-        const int q = warp & 3;            // TMEM lane quarter this warp may read
-        const int hcol = ((warp - 2) >> 2) * HC;  // first tile column of this warp's half
+        const int q = warp & 3;          // TMEM lane quarter this warp may read
+        const int wh = (warp - 2) >> 2;  // which half of the item's columns
         uint8_t* sbuf = sStg + (warp - 2) * Cfg::STG_BYTES;
         int acc = 0;
         uint32_t acc_phase = 0;
-        volatile int* last_flag = abort_flag + 1;
         for (int item = unit; item < p.num_items; item += units) {
-            int t, kb0, kb1, part;
-            tc_item(item, p, num_kb, t, kb0, kb1, part);
+            int t, half;
+            tc_item(item, p, t, half);
             int mb, nb;
             tile_coords(t, p, mb, nb);
+            // This warp's columns of the item: half of them, but at least one
+            // 128-byte chunk (an item that narrow leaves the second warp of
+            // the lane quarter without columns).
+            const int width = half < 0 ? BN : BN / 2;
+            const bool two = width / 2 >= EC;
+            const int wcols = two ? width / 2 : (wh == 0 ? width : 0);
+            const int wcol = two ? wh * (width / 2) : 0;  // offset within the item
             const int row0 = mb * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
             const long long row = (long long)row0 + lane;
-            const long long tcol0 = (long long)nb * BN + hcol;  // this warp's first column
+            const long long tcol0 = (long long)nb * BN + (half > 0 ? BN / 2 : 0) + wcol;
             // Operands that do not depend on the accumulator are fetched before
-            // waiting for it: this half tile's bias and the first residual chunk.
-            const uint4 bias8 = bias_tile_load(tcol0, HC, lane, p.N, p.epi);
+            // waiting for it: this warp's bias and the first residual chunk.
+            const uint4 bias8 = bias_tile_load(tcol0, wcols, lane, p.N, p.epi);
             ResChunk<32, RES> rc;
-            res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, p.epi);
+            if (wcols > 0) res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, p.epi);
             bool ok = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag);
-            // Split items meet at named barriers below, so all four epilogue
-            // warps must take the same branch.
-            ok = part >= 0 ? named_barrier_and<1, 32 * Cfg::EPI_WARPS>(ok) : __all_sync(0xffffffffu, ok);
+            ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + hcol);
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + wcol);
             // Chunks wholly outside C (beyond N, or this warp's 32 rows beyond
             // M) are neither read nor stored.
-            const long long valid_cols = p.N - tcol0 < HC ? (p.N - tcol0 > 0 ? p.N - tcol0 : 0) : HC;
+            long long valid_cols = p.N - tcol0;
+            if (valid_cols > wcols) valid_cols = wcols;
+            if (valid_cols < 0) valid_cols = 0;
             const int nch = row0 < p.M ? (int)((valid_cols + EC - 1) / EC) : 0;
             auto release_accumulator = [&]() {
                 // Whole accumulator read: hand it back to the MMA warp (of the
@@ -349,47 +351,6 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         mbar_arrive(tempty0 + 8u * acc);
                 }
             };
-            // Split tile: park this half's fp32 sums, count in, and let the
-            // second half to arrive finish the tile with other + own.  Two
-            // fp32 terms commute, so the result does not depend on the order.
-            const float* other = nullptr;
-            if (part >= 0) {
-                const int sidx = (t - p.full_items) * (PAIR ? 2 : 1) + (int)rank;
-                const int row_local = q * 32 + lane;
-                float* mine = p.ws + ((size_t)(2 * sidx + part) * 128 + row_local) * BN + hcol;
-                if (row0 < p.M) {
-#pragma unroll 1
-                    for (int c = 0; c < (int)valid_cols; c += 32) {
-                        float w[32];
-                        tmem_ld_32x32b_x32(t_row + (uint32_t)c, w);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4)
-                            __stcg(reinterpret_cast<float4*>(mine + c + i), make_float4(w[i], w[i + 1], w[i + 2], w[i + 3]));
-                    }
-                }
-                __threadfence();
-                named_barrier_sync<1, 32 * Cfg::EPI_WARPS>();
-                if (warp == 2 && lane == 0) {
-                    const int prev = atomicAdd(p.counters + sidx, 1);
-                    const int is_last = prev == 1 ? 1 : 0;
-                    if (is_last) p.counters[sidx] = 0;  // ready for the next launch
-                    *last_flag = is_last;
-                }
-                named_barrier_sync<1, 32 * Cfg::EPI_WARPS>();
-                const bool is_last = *last_flag != 0;
-                named_barrier_sync<1, 32 * Cfg::EPI_WARPS>();  // flag read by all before reuse
-                if (!is_last) {
-                    release_accumulator();
-                    if (++acc == 2) {
-                        acc = 0;
-                        acc_phase ^= 1u;
-                    }
-                    continue;
-                }
-                __threadfence();
-                other = p.ws + ((size_t)(2 * sidx + (part ^ 1)) * 128 + row_local) * BN + hcol;
-            }
             if (nch == 0) release_accumulator();
             // Each chunk is one 128-byte output row per lane (EC columns), built
             // from 32-column sub-chunks: TMEM load, epilogue, GeLU, pack.  Only
@@ -404,16 +365,6 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     tmem_ld_32x32b_x32(t_row + (uint32_t)c, v);
                     tmem_wait_ld();
                     if (ci == nch - 1 && h == EC / 32 - 1) release_accumulator();
-                    if (other != nullptr) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            const float4 o = __ldcg(reinterpret_cast<const float4*>(other + c + i));
-                            v[i] += o.x;
-                            v[i + 1] += o.y;
-                            v[i + 2] += o.z;
-                            v[i + 3] += o.w;
-                        }
-                    }
                     epi_linear<32, RES>(v, rc, bias8, c, p.epi);
                     // The residual registers are free again: start the next
                     // sub-chunk's loads, which then overlap the GeLU math below.
@@ -504,8 +455,7 @@ static bool make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, 
 }
 
 template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
-static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, float* ws, int* counters,
-                                   cudaStream_t stream) {
+static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaStream_t stream) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     const bool f16 = sizeof(OutT) == 2;
     CUtensorMap tA, tB, tC;
@@ -524,13 +474,10 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, float*
     p.num_tiles = p.tiles_m * p.tiles_n;
     p.group_m = PAIR ? 8 : 16;
     p.full_items = plan.full_items;
-    p.split_tiles = plan.split_tiles;
-    p.num_items = plan.full_items + 2 * plan.split_tiles;
-    p.ws = ws;
-    p.counters = counters;
+    p.tail_tiles = plan.tail_tiles;
+    p.num_items = plan.full_items + 2 * plan.tail_tiles;
     p.epi = pr.epi;
-    if (p.num_tiles != plan.full_items + plan.split_tiles || (plan.split_tiles > 0 && (!ws || !counters)))
-        return PAX_ERR_INVALID;
+    if (p.num_tiles != plan.full_items + plan.tail_tiles) return PAX_ERR_INVALID;
 
     auto kern = gemm_tc_kernel<BN, STAGES, OutT, RES, GELU, PAIR>;
     // Attribute is per device; setting it again is cheap and idempotent.
@@ -593,31 +540,29 @@ constexpr int kStagesPair = 6;
 
 // Residual type and GeLU form are compile-time parameters so that each
 // instantiation carries only the epilogue code it runs.
-// Residual type and GeLU form are compile-time parameters so that each
-// instantiation carries only the epilogue code it runs.
 template <int BN, int STAGES, typename OutT, int GELU, bool PAIR>
-static pax_status_t launch_tc_gelu(const Problem& p, const TcPlan& plan, float* ws, int* cnt, cudaStream_t stream) {
-    if (!(p.epi.flags & EPI_RES)) return launch_tc_impl<BN, STAGES, OutT, 0, GELU, PAIR>(p, plan, ws, cnt, stream);
-    if (p.epi.flags & EPI_RES_F32) return launch_tc_impl<BN, STAGES, OutT, 2, GELU, PAIR>(p, plan, ws, cnt, stream);
-    return launch_tc_impl<BN, STAGES, OutT, 1, GELU, PAIR>(p, plan, ws, cnt, stream);
+static pax_status_t launch_tc_gelu(const Problem& p, const TcPlan& plan, cudaStream_t stream) {
+    if (!(p.epi.flags & EPI_RES)) return launch_tc_impl<BN, STAGES, OutT, 0, GELU, PAIR>(p, plan, stream);
+    if (p.epi.flags & EPI_RES_F32) return launch_tc_impl<BN, STAGES, OutT, 2, GELU, PAIR>(p, plan, stream);
+    return launch_tc_impl<BN, STAGES, OutT, 1, GELU, PAIR>(p, plan, stream);
 }
 
 template <int BN, int STAGES, typename OutT, bool PAIR>
-static pax_status_t launch_tc_res(const Problem& p, const TcPlan& plan, float* ws, int* cnt, cudaStream_t stream) {
+static pax_status_t launch_tc_res(const Problem& p, const TcPlan& plan, cudaStream_t stream) {
     // GeLU-tanh uses the hardware tanh when the result is rounded to fp16
     // anyway, and tanhf for fp32 results.
     if (p.epi.flags & EPI_GELU_TANH)
-        return launch_tc_gelu<BN, STAGES, OutT, sizeof(OutT) == 2 ? 3 : 1, PAIR>(p, plan, ws, cnt, stream);
-    if (p.epi.flags & EPI_GELU_ERF) return launch_tc_gelu<BN, STAGES, OutT, 2, PAIR>(p, plan, ws, cnt, stream);
-    return launch_tc_gelu<BN, STAGES, OutT, 0, PAIR>(p, plan, ws, cnt, stream);
+        return launch_tc_gelu<BN, STAGES, OutT, sizeof(OutT) == 2 ? 3 : 1, PAIR>(p, plan, stream);
+    if (p.epi.flags & EPI_GELU_ERF) return launch_tc_gelu<BN, STAGES, OutT, 2, PAIR>(p, plan, stream);
+    return launch_tc_gelu<BN, STAGES, OutT, 0, PAIR>(p, plan, stream);
 }
 
 // plan.shape: 128 / 256 = one CTA per 128 x shape tile; 2 = CTA pair, 256 x 256 tile.
 template <typename OutT>
-static pax_status_t launch_tc_typed(const Problem& p, const TcPlan& plan, float* ws, int* cnt, cudaStream_t stream) {
-    if (plan.shape == 2) return launch_tc_res<256, kStagesPair, OutT, true>(p, plan, ws, cnt, stream);
-    if (plan.shape == 256) return launch_tc_res<256, kStages256, OutT, false>(p, plan, ws, cnt, stream);
-    return launch_tc_res<128, kStages128, OutT, false>(p, plan, ws, cnt, stream);
+static pax_status_t launch_tc_typed(const Problem& p, const TcPlan& plan, cudaStream_t stream) {
+    if (plan.shape == 2) return launch_tc_res<256, kStagesPair, OutT, true>(p, plan, stream);
+    if (plan.shape == 256) return launch_tc_res<256, kStages256, OutT, false>(p, plan, stream);
+    return launch_tc_res<128, kStages128, OutT, false>(p, plan, stream);
 }
 
 static int read_clear_device_error_this_unit() {

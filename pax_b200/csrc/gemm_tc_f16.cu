@@ -3,8 +3,8 @@
 
 namespace pax {
 
-pax_status_t launch_tc_f16(const Problem& p, const TcPlan& plan, float* ws, int* counters, cudaStream_t stream) {
-    return launch_tc_typed<__half>(p, plan, ws, counters, stream);
+pax_status_t launch_tc_f16(const Problem& p, const TcPlan& plan, cudaStream_t stream) {
+    return launch_tc_typed<__half>(p, plan, stream);
 }
 
 int tc_pair_units_f16(int dev, int sms) { return tc_pair_units_typed<__half>(dev, sms); }

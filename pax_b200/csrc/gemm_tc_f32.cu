@@ -3,8 +3,8 @@
 
 namespace pax {
 
-pax_status_t launch_tc_f32(const Problem& p, const TcPlan& plan, float* ws, int* counters, cudaStream_t stream) {
-    return launch_tc_typed<float>(p, plan, ws, counters, stream);
+pax_status_t launch_tc_f32(const Problem& p, const TcPlan& plan, cudaStream_t stream) {
+    return launch_tc_typed<float>(p, plan, stream);
 }
 
 int tc_pair_units_f32(int dev, int sms) { return tc_pair_units_typed<float>(dev, sms); }

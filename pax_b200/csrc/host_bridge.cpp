@@ -240,18 +240,10 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
                 shape = env_int("PAX_TC_BN", 0);
                 if (shape != 128 && shape != 256) shape = tc_pick_bn(p.M, p.N, di.sms);
             }
-            // Splitting the tail wave's tiles along K is off by default: its
-            // fix-up (row-per-lane fp32 partials through global memory) costs
-            // more than the half wave it saves at the sizes measured so far.
-            TcPlan plan = tc_plan(p, shape, dev, di.sms, env_int("PAX_TC_SPLIT", 0) != 0);
-            int* counters = nullptr;
-            float* partials = nullptr;
-            if (plan.split_tiles > 0) {
-                const size_t cnt_pad = (plan.cnt_bytes + 255) & ~size_t(255);
-                if (get_workspace(dev, s, cnt_pad, plan.ws_bytes, &counters, &partials) != PAX_OK)
-                    plan = tc_plan(p, shape, dev, di.sms, false);  // no workspace: whole tiles only
-            }
-            st = launch_tc(p, plan, partials, counters, s);
+            // The tail wave's tiles run as column halves (PAX_TC_HALVES=0
+            // turns that off for comparisons).
+            const TcPlan plan = tc_plan(p, shape, dev, di.sms, env_int("PAX_TC_HALVES", 1) != 0);
+            st = launch_tc(p, plan, s);
             break;
         }
         case PAX_ALGO_SKINNY: {

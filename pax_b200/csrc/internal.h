@@ -33,19 +33,16 @@ bool tma_compatible(const Problem& p);
 // Launch plan of the tcgen05 kernel.  shape: 128 or 256 = one CTA per
 // 128 x shape output tile; 2 = CTA pair (cluster of two, cta_group::2) per
 // 256 x 256 tile.  Tiles [0, full_items) are computed whole; the last
-// split_tiles tiles (the tail wave) are split into two K halves that meet
-// through `ws` (ws_bytes) and per-tile counters (cnt_bytes, zero before the
-// launch and left zero).  units = CTAs (or pairs) launched.
+// tail_tiles tiles (the tail wave) as two column halves each.
+// units = CTAs (or pairs) launched.
 struct TcPlan {
     int shape = 128;
     int units = 0;
     int full_items = 0;
-    int split_tiles = 0;
-    size_t cnt_bytes = 0;
-    size_t ws_bytes = 0;
+    int tail_tiles = 0;
 };
-TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_split);
-pax_status_t launch_tc(const Problem& p, const TcPlan& plan, float* ws, int* counters, cudaStream_t stream);
+TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_halves);
+pax_status_t launch_tc(const Problem& p, const TcPlan& plan, cudaStream_t stream);
 pax_status_t launch_simt(const Problem& p, cudaStream_t stream);
 // Skinny kernel, nt (128, 256 or 512) output columns per work unit: `ws`
 // holds grid*2*MP*nt fp32 partial sums and `counters` one int per nt-column

@@ -355,14 +355,25 @@ def test_no_device_errors_recorded(cuda):
     assert pax_b200.device_error() == pax_b200.Status.OK
 
 
-@pytest.mark.parametrize("shape,algo", [((4096, 4096, 512), "tc2"), ((4096, 4096, 512), "tc"), ((1024, 1024, 1024), "tc"),
-                                        ((1024, 1024, 1024), "tc2"), ((2304, 1280, 200), "tc2"), ((300, 520, 136), "tc")])
+TAIL_SHAPES = [((4096, 4096, 512), "tc2"), ((4096, 4096, 512), "256"), ((4096, 4096, 512), "128"),
+               ((1024, 1024, 1024), "128"), ((1024, 1024, 1024), "tc2"), ((2304, 1280, 200), "tc2"),
+               ((300, 520, 136), "256"), ((2400, 1352, 72), "128")]
+
+
+def _force_tile(monkeypatch, algo):
+    """'tc2' = CTA pair; '128' / '256' = one-CTA tile width."""
+    if algo == "tc2":
+        return "tc2"
+    monkeypatch.setenv("PAX_TC_BN", algo)
+    return "tc"
+
+
+@pytest.mark.parametrize("shape,algo", TAIL_SHAPES)
 @pytest.mark.parametrize("epi", ["bias_gelu_tanh", "residual_gelu_erf"])
-def test_tail_wave_split(cuda, rng, monkeypatch, shape, algo, epi):
-    """Tiles of the tail wave are split in two K halves joined through the
-    workspace (PAX_TC_SPLIT=1); shapes here leave a partial last wave (and odd
-    k-block counts)."""
-    monkeypatch.setenv("PAX_TC_SPLIT", "1")
+def test_tail_wave_halves(cuda, rng, monkeypatch, shape, algo, epi):
+    """Tiles of the tail wave run as two column halves (MMA N = BN/2); the
+    shapes leave a partial last wave, ragged edges and odd k-block counts."""
+    algo = _force_tile(monkeypatch, algo)
     M, N, K = shape
     A, B = inputs(rng, M, N, K)
     bias = rng.standard_normal(N).astype(np.float16)
@@ -372,13 +383,15 @@ def test_tail_wave_split(cuda, rng, monkeypatch, shape, algo, epi):
         check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
 
 
-@pytest.mark.parametrize("algo", ["tc", "tc2"])
-def test_tail_wave_split_bit_exact_and_deterministic(cuda, rng, monkeypatch, algo):
-    monkeypatch.setenv("PAX_TC_SPLIT", "1")
-    A = rng.integers(-3, 4, (1024, 1024)).astype(np.float16)
-    B = rng.integers(-3, 4, (1024, 1024)).astype(np.float16)
+@pytest.mark.parametrize("algo", ["tc2", "256", "128"])
+def test_tail_wave_halves_bit_exact_and_same_as_whole(cuda, rng, monkeypatch, algo):
+    """Integer-valued inputs: every output exact, and identical with the
+    tail halves switched off (PAX_TC_HALVES=0)."""
+    algo = _force_tile(monkeypatch, algo)
+    A = rng.integers(-3, 4, (768, 1024)).astype(np.float16)
+    B = rng.integers(-3, 4, (1024, 1288)).astype(np.float16)
     exact = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.float32)
     first = run_gemm(A, B, cuda, out_dtype=np.float32, algo=algo)
     assert np.array_equal(first, exact)
-    for _ in range(3):
-        assert np.array_equal(run_gemm(A, B, cuda, out_dtype=np.float32, algo=algo), first)
+    monkeypatch.setenv("PAX_TC_HALVES", "0")
+    assert np.array_equal(run_gemm(A, B, cuda, out_dtype=np.float32, algo=algo), first)
