@@ -33,6 +33,7 @@ struct SkinnyParams {
     long long work; // num_tiles * kblocks
     int grid;       // number of CTAs (<= work)
     int slices;     // lockstep layout: K slices per tile (CTA = tile * slices + slice); 0 = stream-K
+    int korder;     // stream-K only: visit the CTA's segments last to first
     float* ws;      // [grid][2][MP][NT] fp32 partial sums
     int* counters;  // [num_tiles], zero between launches
     __half* c16;    // exactly one of c16 / c32 is set
@@ -80,12 +81,18 @@ struct SkSeg {
 };
 
 // Segments of this CTA in order; `cursor` starts at sk_cursor0().
-//   stream-K: the CTA's contiguous unit range [ub, ue), cut at tile edges.
+//   stream-K: the CTA's contiguous unit range [ub, ue), cut at tile edges,
+//             first to last; with korder, last to first.  A range shorter
+//             than a tile then starts with the head (k-blocks 0..) of its
+//             second tile and ends with the tail of its first, so every CTA
+//             reads within (tile k-blocks - range length) k-rows of the same
+//             place in B at any time.
 //   lockstep: one segment, slice s = blockIdx.x % slices of tile
 //             blockIdx.x / slices takes k-blocks s, s + slices, ..., so all
 //             CTAs advance through the same k-rows of B together.
 __device__ __forceinline__ long long sk_cursor0(const SkinnyParams& p) {
-    return p.slices > 0 ? 0 : sk_unit_begin(blockIdx.x, p);
+    if (p.slices > 0) return 0;
+    return p.korder ? sk_unit_begin(blockIdx.x + 1, p) : sk_unit_begin(blockIdx.x, p);
 }
 __device__ __forceinline__ bool sk_next_seg(const SkinnyParams& p, long long& cursor, SkSeg& sg) {
     const int KB = p.kblocks;
@@ -98,6 +105,17 @@ __device__ __forceinline__ bool sk_next_seg(const SkinnyParams& p, long long& cu
         sg.kstep = p.slices;
         sg.nk = sl < KB ? (KB - sl + p.slices - 1) / p.slices : 0;
         return sg.nk > 0;
+    }
+    if (p.korder) {
+        const long long ub = sk_unit_begin(blockIdx.x, p);
+        if (cursor <= ub) return false;
+        sg.tile = (int)((cursor - 1) / KB);
+        const long long seg_begin = max(ub, (long long)sg.tile * KB);
+        sg.kb0 = (int)(seg_begin - (long long)sg.tile * KB);
+        sg.kstep = 1;
+        sg.nk = (int)(cursor - seg_begin);
+        cursor = seg_begin;
+        return true;
     }
     const long long ue = sk_unit_begin(blockIdx.x + 1, p);
     if (cursor >= ue) return false;
@@ -435,8 +453,8 @@ void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int
 }
 
 template <int MP, int NT>
-static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, float* ws, int* counters,
-                                       cudaStream_t stream) {
+static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, bool korder, float* ws,
+                                       int* counters, cudaStream_t stream) {
     using Cfg = SkCfg<MP, NT>;
     CUtensorMap tA, tB;
     if (!sk_tmap(&tA, pr.A, pr.K, pr.M, pr.lda * 2, 64, MP)) return PAX_ERR_CUDA;
@@ -450,6 +468,7 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
     p.work = (long long)p.num_tiles * p.kblocks;
     p.grid = grid;
     p.slices = slices;
+    p.korder = (slices == 0 && korder) ? 1 : 0;
     p.ws = ws;
     p.counters = counters;
     p.c16 = pr.c_f16 ? static_cast<__half*>(pr.C) : nullptr;
@@ -466,24 +485,25 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
 }
 
 template <int NT>
-static pax_status_t launch_skinny_nt(const Problem& p, int grid, int slices, float* ws, int* counters,
+static pax_status_t launch_skinny_nt(const Problem& p, int grid, int slices, bool korder, float* ws, int* counters,
                                      cudaStream_t stream) {
     switch (skinny_mp(p.M)) {
-        case 16: return launch_skinny_impl<16, NT>(p, grid, slices, ws, counters, stream);
-        case 32: return launch_skinny_impl<32, NT>(p, grid, slices, ws, counters, stream);
-        case 48: return launch_skinny_impl<48, NT>(p, grid, slices, ws, counters, stream);
-        default: return launch_skinny_impl<64, NT>(p, grid, slices, ws, counters, stream);
+        case 16: return launch_skinny_impl<16, NT>(p, grid, slices, korder, ws, counters, stream);
+        case 32: return launch_skinny_impl<32, NT>(p, grid, slices, korder, ws, counters, stream);
+        case 48: return launch_skinny_impl<48, NT>(p, grid, slices, korder, ws, counters, stream);
+        default: return launch_skinny_impl<64, NT>(p, grid, slices, korder, ws, counters, stream);
     }
 }
 
 // nt: 128 or 256 output columns per unit.  slices > 0: lockstep layout (nt
-// 128, grid = tiles x slices); 0: persistent stream-K over `grid` CTAs.
+// 128, grid = tiles x slices); 0: persistent stream-K over `grid` CTAs,
+// segments in k order when korder is set.
 pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, int* counters, cudaStream_t stream,
-                              int slices) {
+                              int slices, bool korder) {
     if (p.M < 1 || p.M > kSkinnyMaxM || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
-    if (slices > 0) return launch_skinny_nt<128>(p, grid, slices, ws, counters, stream);
-    if (nt == 256) return launch_skinny_nt<256>(p, grid, 0, ws, counters, stream);
-    return launch_skinny_nt<128>(p, grid, 0, ws, counters, stream);
+    if (slices > 0) return launch_skinny_nt<128>(p, grid, slices, false, ws, counters, stream);
+    if (nt == 256) return launch_skinny_nt<256>(p, grid, 0, korder, ws, counters, stream);
+    return launch_skinny_nt<128>(p, grid, 0, korder, ws, counters, stream);
 }
 
 int read_clear_device_error_skinny() {

@@ -12,6 +12,9 @@ int read_clear_device_error_tc_f16();
 int read_clear_device_error_tc_f32();
 
 size_t tc_smem_bytes(int shape, bool c_f16) {
+    if (shape == 4)
+        return c_f16 ? TcCfg<512, kStagesWide, __half, true>::SMEM_BYTES
+                     : TcCfg<512, kStagesWide, float, true>::SMEM_BYTES;
     if (shape == 2)
         return c_f16 ? TcCfg<256, kStagesPair, __half, true>::SMEM_BYTES
                      : TcCfg<256, kStagesPair, float, true>::SMEM_BYTES;
@@ -31,27 +34,48 @@ int tc_pick_bn(long long M, long long N, int sms) {
     return 128;
 }
 
-// Tile shape by a wave-count cost model.  Time ~ waves x (work of one tile
-// per SM) / (relative per-SM throughput of the shape); the throughputs are
-// measured ratios on B200 (128x256 tiles = 1, CTA-pair 256x256 = 1.04,
-// 128x128 = 0.67).
-int tc_pick_shape(long long M, long long N, int sms) {
+// Tile shape by a wave-count cost model.  Time ~ rounds x (time of one
+// tile on its SM or pair); time unit: one 128 x 256 x K tile on one SM at
+// the one-CTA kernel's rate.  Relative mainloop throughputs measured on
+// B200 (4096^3 and 8192^3): 128 x 128 = 0.67, CTA pair 256 x 256 = 1.10,
+// wide pair 256 x 512 = 1.32.  The wide tile has a single accumulator, so
+// its epilogue is not hidden behind the next tile: it adds a per-tile term
+// that grows with the epilogue's work and shrinks with K (fitted: 0.03 of a
+// unit at K = 4096 for bias / tanh-GeLU, 0.43 with residual and erf-GeLU).
+// Tail waves of at most half the units run as column halves.
+static double tc_rounds(long long tiles, long long units) {
+    const long long full = tiles / units, rem = tiles % units;
+    if (rem == 0) return (double)full;
+    return (double)full + (2 * rem <= units ? 0.5 : 1.0);
+}
+
+int tc_pick_shape(const Problem& p, int sms) {
     const long long pairs = sms / 2;  // resident pairs are refined at launch (tc_pair_units)
-    auto waves = [](long long tiles, long long units) { return (tiles + units - 1) / units; };
-    const double t256 = (double)waves(((M + 127) / 128) * ((N + 255) / 256), sms) * 1.0;
-    const double t128 = (double)waves(((M + 127) / 128) * ((N + 127) / 128), sms) * 0.5 / 0.67;
-    const double tpair = (double)waves(((M + 255) / 256) * ((N + 255) / 256), pairs) * 1.0 / 1.04;
-    if (tpair <= t256 && tpair <= t128) return 2;
-    return t256 <= t128 ? 256 : 128;
+    const long long M = p.M, N = p.N;
+    const long long tm = (M + 127) / 128, tm2 = (M + 255) / 256;
+    const double t256 = tc_rounds(tm * ((N + 255) / 256), sms);
+    const double t128 = tc_rounds(tm * ((N + 127) / 128), sms) * 0.5 / 0.67;
+    const double tpair = tc_rounds(tm2 * ((N + 255) / 256), pairs) / 1.10;
+    const int f = p.epi.flags;
+    const double epi = 0.03 + ((f & EPI_RES) ? 0.2 : 0.0) + ((f & EPI_GELU_ERF) ? 0.2 : 0.0);
+    const double kscale = 4096.0 / (double)(p.K > 64 ? p.K : 64);
+    const double twide = tc_rounds(tm2 * ((N + 511) / 512), pairs) * (2.0 / 1.32 + epi * kscale);
+    double best = t256;
+    int shape = 256;
+    if (t128 < best) { best = t128; shape = 128; }
+    if (tpair <= best) { best = tpair; shape = 2; }
+    if (twide < best) { best = twide; shape = 4; }
+    return shape;
 }
 
 TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_halves) {
     TcPlan plan;
-    plan.shape = (shape == 2 || shape == 256) ? shape : 128;
-    const long long tile_m = plan.shape == 2 ? 256 : 128;
-    const long long tile_n = plan.shape == 128 ? 128 : 256;
+    plan.shape = (shape == 2 || shape == 4 || shape == 256) ? shape : 128;
+    const bool pair = plan.shape == 2 || plan.shape == 4;
+    const long long tile_m = pair ? 256 : 128;
+    const long long tile_n = plan.shape == 4 ? 512 : plan.shape == 128 ? 128 : 256;
     const long long tiles = ((p.M + tile_m - 1) / tile_m) * ((p.N + tile_n - 1) / tile_n);
-    const long long max_units = plan.shape == 2 ? tc_pair_units_f16(dev, sms) : sms;
+    const long long max_units = pair ? tc_pair_units_f16(dev, sms) : sms;
     // The tail wave: tiles left after whole waves.  When at most half the
     // units would be busy on them, each is cut into two column halves, so
     // the tail takes about half the time of a wave.

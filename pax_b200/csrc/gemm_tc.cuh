@@ -68,9 +68,17 @@ __device__ __forceinline__ void tc_item(int item, const TcParams& p, int& tile, 
 // CTA stages its own 128 rows of A and BN/2 columns of B, and holds its 128
 // rows of the accumulator in its own TMEM.  A column-half item is the same
 // with BN/2 accumulator columns (MMA N = BN/2).
+// BN = 512 (pair only, "wide"): the pair computes a 256 x 512 tile as two
+// N = 256 MMAs per k-step that share A, into one accumulator filling all 512
+// TMEM columns (no second accumulator buffer).  Each CTA stages B columns
+// [rank*128, +128) and [256 + rank*128, +128) of the tile.  Fewer staged
+// bytes per MMA than the 256 x 256 tile; the epilogue is not overlapped with
+// the next tile's MMAs.  Its column halves are single N = 256 MMAs.
 template <int BN_, int STAGES_, typename OutT, bool PAIR_>
 struct TcCfg {
     static constexpr bool PAIR = PAIR_;
+    static constexpr bool WIDE = BN_ == 512;
+    static constexpr int MMA_N = WIDE ? 256 : BN_;       // N of one MMA instruction
     static constexpr int BM = 128;                       // rows per CTA
     static constexpr int BN = BN_;                       // accumulator columns (MMA N)
     static constexpr int BN_LOCAL = PAIR ? BN / 2 : BN;  // B columns staged per CTA
@@ -86,15 +94,17 @@ struct TcCfg {
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr uint32_t STG_BYTES = 32 * 128;            // per warp
     static constexpr uint32_t STG_TOTAL = EPI_WARPS * STG_BYTES;
-    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr int ACC_BUFS = WIDE ? 1 : 2;        // accumulator buffers in TMEM
+    static constexpr uint32_t TMEM_COLS = ACC_BUFS * BN;
     static constexpr uint32_t NUM_BARS = 2 * STAGES + 5;
     static constexpr size_t SMEM_BYTES =
         1024 + (size_t)STAGES * STAGE_BYTES + STG_TOTAL + NUM_BARS * 8 + 16;
-    static constexpr uint32_t IDESC = umma_idesc_f16(PAIR ? 256 : 128, BN, /*a_mn*/ false, /*b_mn*/ true);
-    static constexpr uint32_t IDESC_HALF = umma_idesc_f16(PAIR ? 256 : 128, BN / 2, false, true);
+    static constexpr uint32_t IDESC = umma_idesc_f16(PAIR ? 256 : 128, MMA_N, /*a_mn*/ false, /*b_mn*/ true);
+    static constexpr uint32_t IDESC_HALF = umma_idesc_f16(PAIR ? 256 : 128, WIDE ? 256 : BN / 2, false, true);
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
     static_assert((BN_LOCAL / 2) % 64 == 0, "B (and a half of it) is staged in 64-column boxes");
+    static_assert(!WIDE || PAIR, "the wide tile is a CTA-pair tile");
 };
 
 __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& mb, int& nb) {
@@ -203,8 +213,13 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         const uint32_t fb_leader = mapa_shared(fb, 0);
                         if (leader) mbar_arrive_expect_tx(fb, 2 * bytes);
                         tma_load_2d_pair(adst, &tmA, fb_leader, kb * Cfg::BK, arow);
-                        for (int j = 0; j < wl / 64; ++j)
-                            tma_load_2d_pair(bdst + j * 8192, &tmB, fb_leader, bcol + j * 64, kb * Cfg::BK);
+                        for (int j = 0; j < wl / 64; ++j) {
+                            // Wide tile: boxes 0-1 feed the MMA for item columns
+                            // [0, 256), boxes 2-3 the one for [256, 512).
+                            const int col = Cfg::WIDE ? ncol0 + (j >> 1) * 256 + (int)rank * 128 + (j & 1) * 64
+                                                      : bcol + j * 64;
+                            tma_load_2d_pair(bdst + j * 8192, &tmB, fb_leader, col, kb * Cfg::BK);
+                        }
                     } else {
                         mbar_arrive_expect_tx(fb, bytes);
                         tma_load_2d(adst, &tmA, fb, kb * Cfg::BK, arow);
@@ -252,6 +267,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                 if (!mbar_wait<PAIR>(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                const bool two = Cfg::WIDE && half < 0;  // wide whole tile: two N = 256 MMAs per k-step
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(full0 + 8u * stage, phase, abort_flag)) {
                         ok = false;
@@ -264,10 +280,14 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
                         const uint64_t ad = as + (uint64_t)((kk * 32) >> 4);    // +32 B along K
                         const uint64_t bd = bs + (uint64_t)((kk * 2048) >> 4);  // +16 rows of K
-                        if constexpr (PAIR)
+                        if constexpr (PAIR) {
                             tc_mma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
-                        else
+                            if (two)
+                                tc_mma_f16_pair(d_tmem + 256u, ad, bd + (uint64_t)((2 * 8192) >> 4), idesc,
+                                                (kb | kk) != 0 ? 1u : 0u);
+                        } else {
                             tc_mma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+                        }
                     }
                     if constexpr (PAIR) {
                         tc_commit_pair(mapa_shared(empty0 + 8u * stage, 0));
@@ -287,7 +307,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                 } else {
                     tc_commit(tfull0 + 8u * acc);
                 }
-                if (++acc == 2) {
+                if (++acc == Cfg::ACC_BUFS) {
                     acc = 0;
                     acc_phase ^= 1u;
                 }
@@ -398,7 +418,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     bulk_commit();
                 }
             }
-            if (++acc == 2) {
+            if (++acc == Cfg::ACC_BUFS) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
@@ -537,6 +557,7 @@ static int tc_pair_units_typed(int dev, int sms) {
 constexpr int kStages256 = 4;
 constexpr int kStages128 = 6;
 constexpr int kStagesPair = 6;
+constexpr int kStagesWide = 4;
 
 // Residual type and GeLU form are compile-time parameters so that each
 // instantiation carries only the epilogue code it runs.
@@ -557,9 +578,11 @@ static pax_status_t launch_tc_res(const Problem& p, const TcPlan& plan, cudaStre
     return launch_tc_gelu<BN, STAGES, OutT, 0, PAIR>(p, plan, stream);
 }
 
-// plan.shape: 128 / 256 = one CTA per 128 x shape tile; 2 = CTA pair, 256 x 256 tile.
+// plan.shape: 128 / 256 = one CTA per 128 x shape tile; 2 = CTA pair, 256 x 256
+// tile; 4 = CTA pair, 256 x 512 tile.
 template <typename OutT>
 static pax_status_t launch_tc_typed(const Problem& p, const TcPlan& plan, cudaStream_t stream) {
+    if (plan.shape == 4) return launch_tc_res<512, kStagesWide, OutT, true>(p, plan, stream);
     if (plan.shape == 2) return launch_tc_res<256, kStagesPair, OutT, true>(p, plan, stream);
     if (plan.shape == 256) return launch_tc_res<256, kStages256, OutT, false>(p, plan, stream);
     return launch_tc_res<128, kStages128, OutT, false>(p, plan, stream);

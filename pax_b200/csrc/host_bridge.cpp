@@ -223,10 +223,10 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
     if (algo == PAX_ALGO_AUTO) {
         algo = select_algo(p);
         if (algo == PAX_ALGO_TC) {
-            shape = tc_pick_shape(p.M, p.N, di.sms);
+            shape = tc_pick_shape(p, di.sms);
             const int forced = env_int("PAX_TC_SHAPE", 0);
-            if (forced == 2 || forced == 128 || forced == 256) shape = forced;
-            if (shape == 2) algo = PAX_ALGO_TC2;
+            if (forced == 2 || forced == 4 || forced == 128 || forced == 256) shape = forced;
+            if (shape == 2 || shape == 4) algo = PAX_ALGO_TC2;
         }
     }
     pax_status_t st;
@@ -235,7 +235,7 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
         case PAX_ALGO_TC2: {
             if (!tma_compatible(p)) return fail(PAX_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned rows");
             if (algo == PAX_ALGO_TC2) {
-                shape = 2;
+                if (shape != 4) shape = 2;
             } else if (shape != 128 && shape != 256) {
                 shape = env_int("PAX_TC_BN", 0);
                 if (shape != 128 && shape != 256) shape = tc_pick_bn(p.M, p.N, di.sms);
@@ -252,8 +252,10 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
                             kSkinnyMaxM);
             // Lockstep layout when there are no more column tiles than SMs;
             // otherwise persistent stream-K, one CTA per SM.
-            // PAX_SKINNY_NT=128|256 forces the persistent layout.
+            // PAX_SKINNY_NT=128|256 forces the persistent layout;
+            // PAX_SKINNY_KORDER=1 visits its segments in k order.
             int nt = env_int("PAX_SKINNY_NT", 0);
+            const bool korder = env_int("PAX_SKINNY_KORDER", 0) != 0;
             const int slices = (nt == 0) ? skinny_lockstep_slices(p.N, p.K, di.sms) : 0;
             const bool lockstep = slices > 0;
             if (lockstep) nt = 128;
@@ -271,7 +273,7 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
             float* partials = nullptr;
             st = get_workspace(dev, s, cnt_pad, ws_bytes, &counters, &partials);
             if (st != PAX_OK) return fail(st, "skinny workspace allocation failed (%zu bytes)", cnt_pad + ws_bytes);
-            st = launch_skinny_ws(p, nt, grid, partials, counters, s, slices);
+            st = launch_skinny_ws(p, nt, grid, partials, counters, s, slices, korder);
             break;
         }
         case PAX_ALGO_SIMT: st = launch_simt(p, s); break;
@@ -357,7 +359,7 @@ pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc) {
     int dev = 0, sms = 0;
     if (a == PAX_ALGO_TC && cudaGetDevice(&dev) == cudaSuccess &&
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0 &&
-        tc_pick_shape(p.M, p.N, sms) == 2)
+        (tc_pick_shape(p, sms) == 2 || tc_pick_shape(p, sms) == 4))
         a = PAX_ALGO_TC2;
     cudaGetLastError();  // no device here is not an error of this call
     return a;

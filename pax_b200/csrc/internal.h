@@ -32,7 +32,7 @@ bool tma_compatible(const Problem& p);
 // Launchers.  Each returns PAX_OK or an error status; none synchronises.
 // Launch plan of the tcgen05 kernel.  shape: 128 or 256 = one CTA per
 // 128 x shape output tile; 2 = CTA pair (cluster of two, cta_group::2) per
-// 256 x 256 tile.  Tiles [0, full_items) are computed whole; the last
+// 256 x 256 tile; 4 = CTA pair per 256 x 512 tile.  Tiles [0, full_items) are computed whole; the last
 // tail_tiles tiles (the tail wave) as two column halves each.
 // units = CTAs (or pairs) launched.
 struct TcPlan {
@@ -54,16 +54,18 @@ void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int
                      size_t* counter_bytes);
 // slices > 0 = the lockstep layout (nt 128, `grid` = tiles x slices CTAs,
 // one per SM); its workspace is sized by skinny_geometry with that grid's
-// per-CTA share.  slices = 0: persistent stream-K.
+// per-CTA share.  slices = 0: persistent stream-K, each CTA's segments in
+// k order (its later tile's head first) when korder is set.
 pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, int* counters, cudaStream_t stream,
-                              int slices = 0);
+                              int slices = 0, bool korder = false);
 
 // Dynamic shared memory of the tcgen05 kernel for a tile shape / output type.
 size_t tc_smem_bytes(int shape, bool c_f16);
 // Tile width of the one-CTA shape for a problem (128 or 256).
 int tc_pick_bn(long long M, long long N, int sms);
-// Tile shape pax_gemm_ex picks by itself: 128, 256 (one CTA) or 2 (pair).
-int tc_pick_shape(long long M, long long N, int sms);
+// Tile shape pax_gemm_ex picks by itself: 128, 256 (one CTA), 2 (pair,
+// 256 x 256) or 4 (pair, 256 x 512).
+int tc_pick_shape(const Problem& p, int sms);
 // Largest M the skinny kernel accepts.
 constexpr long long kSkinnyMaxM = 64;
 

@@ -113,14 +113,16 @@ def test_skinny(cuda, rng, M, NK):
     check(got, oracle.gemm(A, B, epi="bias", bias=bias, out_dtype=np.float16), np.float16)
 
 
-@pytest.mark.parametrize("nt", [0, 128, 256])
+@pytest.mark.parametrize("nt,korder", [(0, 0), (128, 0), (256, 0), (128, 1), (256, 1)])
 @pytest.mark.parametrize("M,N,K", [(16, 16384, 4096), (1, 1000, 320), (33, 2048, 1088), (64, 768, 4096),
                                    (16, 520, 64), (16, 40960, 2048), (48, 16384, 4160)])
-def test_skinny_layouts(cuda, rng, monkeypatch, nt, M, N, K):
+def test_skinny_layouts(cuda, rng, monkeypatch, nt, korder, M, N, K):
     """Lockstep layout (nt=0: one CTA per (tile, interleaved K slice)) and the
-    persistent stream-K layout with 128- and 256-column units, including
-    ragged N, uneven K slices and tiles split between CTAs."""
+    persistent stream-K layout with 128- and 256-column units, segments
+    first-to-last or in k order (korder), including ragged N, uneven K
+    slices and tiles split between CTAs."""
     monkeypatch.setenv("PAX_SKINNY_NT", str(nt))
+    monkeypatch.setenv("PAX_SKINNY_KORDER", str(korder))
     A, B = inputs(rng, M, N, K, dist="normal")
     bias = rng.standard_normal(N).astype(np.float16)
     got = run_gemm(A, B, cuda, epi="bias", bias=bias, out_dtype=np.float16, algo="skinny")
@@ -136,6 +138,21 @@ def test_skinny_epilogues(cuda, rng, epi, out):
     res = rng.standard_normal((M, N)).astype(np.float16)
     got = run_gemm(A, B, cuda, epi=epi, bias=bias, residual=res, out_dtype=out, algo="skinny")
     check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
+
+
+@pytest.mark.parametrize("korder", [0, 1])
+def test_skinny_stream_k_bit_exact_and_deterministic(cuda, rng, monkeypatch, korder):
+    """Integer-valued inputs through stream-K with split tiles: exact, and
+    the same bits on every run (partials are summed in CTA order)."""
+    monkeypatch.setenv("PAX_SKINNY_NT", "128")
+    monkeypatch.setenv("PAX_SKINNY_KORDER", str(korder))
+    A = rng.integers(-3, 4, (16, 4096)).astype(np.float16)
+    B = rng.integers(-3, 4, (4096, 16384)).astype(np.float16)
+    exact = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.float32)
+    first = run_gemm(A, B, cuda, out_dtype=np.float32, algo="skinny")
+    assert np.array_equal(first, exact)
+    for _ in range(2):
+        assert np.array_equal(run_gemm(A, B, cuda, out_dtype=np.float32, algo="skinny"), first)
 
 
 def test_skinny_workspace_reuse_across_shapes(cuda, rng):
@@ -357,13 +374,18 @@ def test_no_device_errors_recorded(cuda):
 
 TAIL_SHAPES = [((4096, 4096, 512), "tc2"), ((4096, 4096, 512), "256"), ((4096, 4096, 512), "128"),
                ((1024, 1024, 1024), "128"), ((1024, 1024, 1024), "tc2"), ((2304, 1280, 200), "tc2"),
-               ((300, 520, 136), "256"), ((2400, 1352, 72), "128")]
+               ((300, 520, 136), "256"), ((2400, 1352, 72), "128"), ((4096, 4096, 512), "wide"),
+               ((2304, 1280, 200), "wide"), ((300, 1040, 136), "wide"), ((9984, 3592, 64), "wide")]
 
 
 def _force_tile(monkeypatch, algo):
-    """'tc2' = CTA pair; '128' / '256' = one-CTA tile width."""
+    """'tc2' = CTA pair; 'wide' = CTA pair with 256 x 512 tiles; '128' /
+    '256' = one-CTA tile width."""
     if algo == "tc2":
         return "tc2"
+    if algo == "wide":
+        monkeypatch.setenv("PAX_TC_SHAPE", "4")
+        return "auto"
     monkeypatch.setenv("PAX_TC_BN", algo)
     return "tc"
 
@@ -383,7 +405,7 @@ def test_tail_wave_halves(cuda, rng, monkeypatch, shape, algo, epi):
         check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
 
 
-@pytest.mark.parametrize("algo", ["tc2", "256", "128"])
+@pytest.mark.parametrize("algo", ["tc2", "wide", "256", "128"])
 def test_tail_wave_halves_bit_exact_and_same_as_whole(cuda, rng, monkeypatch, algo):
     """Integer-valued inputs: every output exact, and identical with the
     tail halves switched off (PAX_TC_HALVES=0)."""
@@ -395,3 +417,19 @@ def test_tail_wave_halves_bit_exact_and_same_as_whole(cuda, rng, monkeypatch, al
     assert np.array_equal(first, exact)
     monkeypatch.setenv("PAX_TC_HALVES", "0")
     assert np.array_equal(run_gemm(A, B, cuda, out_dtype=np.float32, algo=algo), first)
+
+
+@pytest.mark.parametrize("epi", ["none", "bias", "bias_gelu_tanh", "bias_gelu_erf", "residual_gelu_tanh",
+                                 "residual_gelu_erf"])
+@pytest.mark.parametrize("out", [np.float16, np.float32])
+@pytest.mark.parametrize("shape", [(512, 1024, 256), (1000, 1480, 328), (256, 512, 64)])
+def test_wide_tile_epilogues(cuda, rng, monkeypatch, epi, out, shape):
+    """The 256 x 512 CTA-pair tile: every epilogue, both output types, whole
+    and ragged tiles."""
+    monkeypatch.setenv("PAX_TC_SHAPE", "4")
+    M, N, K = shape
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    res = rng.standard_normal((M, N)).astype(np.float16)
+    got = run_gemm(A, B, cuda, epi=epi, bias=bias, residual=res, out_dtype=out)
+    check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
