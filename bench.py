@@ -405,6 +405,8 @@ def run_pax(args):
     e2e_value = flops_total / (float(t.item()) * 1e-3) / 1e12
 
     peak, hbm, peak_kind = peaks()
+    stages = pax_b200.pipeline_stages(A, B, C, epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None,
+                                      residual=res)
     kernel_ms = None if gathered else min(ms)
     achieved = None if gathered else flops_rank / (statistics.mean(ms) * 1e-3) / 1e12
     roofline = None
@@ -420,7 +422,7 @@ def run_pax(args):
             roofline = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                         "traffic": traffic_from_profiles(args.config),
                         "peak_kind": f"{peak_kind} (copy bandwidth)", "algorithmic_bytes_per_launch": alg_bytes,
-                        "tflops": achieved}
+                        "tflops": achieved, "best_launch_ms": kernel_ms}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, dt, rows, threads, kind, _ = cpu_gemm_sample(cfg, args.cpu_seconds, args.seed)
@@ -450,8 +452,9 @@ def run_pax(args):
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "clocks": clk,
             "gpu_launches": args.steps,
-            "lean_pipeline_bound": {"stages": 4, "bound_frac": 1 - 1 / 4,
-                                    "measured_frac_of_roof": (value / world) / peak},
+            "lean_pipeline_bound": {"stages": stages, "bound_frac": (1 - 1 / stages) if stages else None,
+                                    "measured_frac_of_roof": roofline["frac"] if roofline else None,
+                                    "holds": (roofline["frac"] >= 1 - 1 / stages) if (roofline and stages) else None},
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -211,6 +211,14 @@ pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cudaStream_t s
  * host-only, launches nothing). */
 pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc);
 
+/* Shared-memory pipeline depth (TMA ring stages) of the kernel pax_gemm_ex
+ * would launch for desc with algo = PAX_ALGO_AUTO on the current device; 0
+ * for the CUDA-core kernel or without a device (new: no counterpart in the
+ * reference; it lets a caller evaluate the reference's pipeline bound
+ * throughput >= (1 - 1/STAGES) * min(compute, memory) for the kernel that
+ * actually runs).  Host-only, launches nothing. */
+int pax_gemm_pipeline_stages(const pax_gemm_desc_t* desc);
+
 /* ---------------------------------------------------------------------------
  * Host bridge (src/host_bridge.c).
  * ------------------------------------------------------------------------- */

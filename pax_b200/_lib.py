@@ -79,6 +79,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "pax_gemm_residual_gelu_erf_f16_launch": ([P, P, P, i, i, i, P, P], None),
         "pax_gemm_ex": ([ctypes.POINTER(GemmDesc), P], i),
         "pax_gemm_select_algo": ([ctypes.POINTER(GemmDesc)], i),
+        "pax_gemm_pipeline_stages": ([ctypes.POINTER(GemmDesc)], i),
         "pax_gemm_skinny_noalloc": ([ctypes.POINTER(GemmDesc), P], i),
         # bridge
         "pax_validate_buffer": ([buf_p], i),

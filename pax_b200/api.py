@@ -124,6 +124,13 @@ def select_algo(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, **kw) -> Algo
     return Algo(_lib.get().pax_gemm_select_algo(ctypes.byref(d)))
 
 
+def pipeline_stages(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, **kw) -> int:
+    """TMA ring depth of the kernel pax_gemm_ex would run (host-only; 0 for
+    the CUDA-core kernel)."""
+    d = make_desc(A, B, C, **kw)
+    return int(_lib.get().pax_gemm_pipeline_stages(ctypes.byref(d)))
+
+
 def device_error() -> Status:
     """Read and clear the device error word (synchronises the device)."""
     return Status(_lib.get().pax_device_error())

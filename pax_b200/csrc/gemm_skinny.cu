@@ -416,6 +416,15 @@ static bool sk_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
 
 int skinny_mp(long long M) { return (int)((M + 15) / 16) * 16; }
 
+int skinny_stages(long long M, int nt) {
+    const int mp = skinny_mp(M);
+    if (nt == 256)
+        return mp == 16 ? SkCfg<16, 256>::STAGES : mp == 32 ? SkCfg<32, 256>::STAGES
+                         : mp == 48 ? SkCfg<48, 256>::STAGES : SkCfg<64, 256>::STAGES;
+    return mp == 16 ? SkCfg<16, 128>::STAGES : mp == 32 ? SkCfg<32, 128>::STAGES
+                     : mp == 48 ? SkCfg<48, 128>::STAGES : SkCfg<64, 128>::STAGES;
+}
+
 int skinny_pick_nt(long long M, long long N, long long K, int sms) {
     const long long kb = (K + 63) / 64;
     (void)M;

@@ -11,6 +11,10 @@ int tc_pair_units_f16(int dev, int sms);
 int read_clear_device_error_tc_f16();
 int read_clear_device_error_tc_f32();
 
+int tc_stages(int shape) {
+    return shape == 4 ? kStagesWide : shape == 2 ? kStagesPair : shape == 256 ? kStages256 : kStages128;
+}
+
 size_t tc_smem_bytes(int shape, bool c_f16) {
     if (shape == 4)
         return c_f16 ? TcCfg<512, kStagesWide, __half, true>::SMEM_BYTES

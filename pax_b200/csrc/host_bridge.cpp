@@ -365,6 +365,33 @@ pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc) {
     return a;
 }
 
+int pax_gemm_pipeline_stages(const pax_gemm_desc_t* desc) {
+    Problem p;
+    if (normalize(desc, &p) != PAX_OK) return 0;
+    set_status(PAX_OK);
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    // The same choices as run() makes for PAX_ALGO_AUTO.
+    const pax_algo_t a = select_algo(p);
+    if (a == PAX_ALGO_TC) {
+        int shape = tc_pick_shape(p, sms);
+        const int forced = env_int("PAX_TC_SHAPE", 0);
+        if (forced == 2 || forced == 4 || forced == 128 || forced == 256) shape = forced;
+        return tc_stages(shape);
+    }
+    if (a == PAX_ALGO_SKINNY) {
+        int nt = env_int("PAX_SKINNY_NT", 0);
+        if (nt == 0 && skinny_lockstep_slices(p.N, p.K, sms) > 0) nt = 128;
+        if (nt != 128 && nt != 256) nt = skinny_pick_nt(p.M, p.N, p.K, sms);
+        return skinny_stages(p.M, nt);
+    }
+    return 0;  // CUDA-core kernel: no TMA ring
+}
+
 // ======================================================= reference launchers
 void pax_gemm_wmma_launch(const __half* A, const __half* B, float* C, int m, int n, int k, cudaStream_t s) {
     gemm_simple(A, B, C, m, n, k, PAX_DT_F32, PAX_EPI_NONE, 1.f, nullptr, nullptr, PAX_DT_F32, s,

@@ -59,6 +59,9 @@ void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int
 pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, int* counters, cudaStream_t stream,
                               int slices = 0, bool korder = false);
 
+// Shared-memory pipeline depth (TMA ring stages) of each kernel variant.
+int tc_stages(int shape);
+int skinny_stages(long long M, int nt);
 // Dynamic shared memory of the tcgen05 kernel for a tile shape / output type.
 size_t tc_smem_bytes(int shape, bool c_f16);
 // Tile width of the one-CTA shape for a problem (128 or 256).
