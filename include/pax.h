@@ -207,6 +207,21 @@ pax_status_t pax_gemm_ex(const pax_gemm_desc_t* desc, cudaStream_t stream);
  * process) on the same device race and give wrong results. */
 pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cudaStream_t stream);
 
+/* Batched GEMM (new; generalises the reference's Futhark entry
+ * pax_batch_gemm, src/pax_kernel.fut:27-28,35, to strided items and every
+ * epilogue): `batch` independent problems C_b = epi(alpha * A_b . B_b) of
+ * the shape, leading dimensions and epilogue in `gemm`, whose pointers
+ * address item 0.  Item b's operands start stride_* elements after item
+ * b-1's.  A stride of 0 shares one A, B, bias or residual between all items;
+ * C items must not overlap.  The tensor-core kernel runs a whole batch in one
+ * launch; m <= 64 and TMA-unaligned problems run one launch per item. */
+typedef struct {
+    pax_gemm_desc_t gemm;
+    int64_t batch;
+    int64_t stride_a, stride_b, stride_c, stride_bias, stride_residual; /* elements */
+} pax_gemm_batched_desc_t;
+pax_status_t pax_gemm_batched_ex(const pax_gemm_batched_desc_t* desc, cudaStream_t stream);
+
 /* The algorithm pax_gemm_ex would run for desc with algo = PAX_ALGO_AUTO (new;
  * host-only, launches nothing). */
 pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc);
@@ -218,6 +233,29 @@ pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc);
  * throughput >= (1 - 1/STAGES) * min(compute, memory) for the kernel that
  * actually runs).  Host-only, launches nothing. */
 int pax_gemm_pipeline_stages(const pax_gemm_desc_t* desc);
+
+/* ---- Lean-extraction symbols (pax-lean4/PAX/Extraction.lean:32-84) ----
+ * The names and signatures PAX's Lean layer exports.  Sizes are 64-bit and
+ * device pointers are passed as integers: A fp16 [M][K], B fp16 [K][N],
+ * C fp32 [M][N], bias fp16 [N], residual fp32 [M][N].  The GEMMs run the
+ * same kernels as pax_gemm_ex on the legacy default stream (asynchronous);
+ * errors go to pax_last_error() and stderr, as for the launchers. */
+void pax_gemm_wmma_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C);
+void pax_gemm_ptx_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C);
+void pax_gemm_pipeline3_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C);
+void pax_gemm_bias_gelu_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C,
+                                 uint64_t bias);
+void pax_gemm_residual_gelu_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C,
+                                     uint64_t residual);
+
+/* IEEE-754 binary16 add, multiply and fused multiply-add with a single
+ * round-to-nearest-even (host code; Extraction.lean:58-84 with
+ * Float16.add/mul/fma of pax-lean4/PAX/Float16.lean:99-125).  NaN results
+ * are 0x7C01, the Lean model's Float16.posNaN.  Signed zeros, infinities and
+ * the overflow threshold (65520) follow IEEE 754. */
+uint16_t pax_fp16_add_verified(uint16_t x, uint16_t y);
+uint16_t pax_fp16_mul_verified(uint16_t x, uint16_t y);
+uint16_t pax_fp16_fma_verified(uint16_t x, uint16_t y, uint16_t z);
 
 /* ---------------------------------------------------------------------------
  * Host bridge (src/host_bridge.c).

@@ -51,6 +51,19 @@ class GemmDesc(ctypes.Structure):
     ]
 
 
+class GemmBatchedDesc(ctypes.Structure):
+    """pax_gemm_batched_desc_t (include/pax.h)."""
+    _fields_ = [
+        ("gemm", GemmDesc),
+        ("batch", ctypes.c_int64),
+        ("stride_a", ctypes.c_int64),
+        ("stride_b", ctypes.c_int64),
+        ("stride_c", ctypes.c_int64),
+        ("stride_bias", ctypes.c_int64),
+        ("stride_residual", ctypes.c_int64),
+    ]
+
+
 def _declare(L: ctypes.CDLL) -> None:
     P = ctypes.c_void_p
     i = ctypes.c_int
@@ -58,6 +71,7 @@ def _declare(L: ctypes.CDLL) -> None:
     sz = ctypes.c_size_t
     buf_p = ctypes.POINTER(PaxBuffer)
     launch7 = [P, P, P, i, i, i, P]
+    u64, u16 = ctypes.c_uint64, ctypes.c_uint16
     sigs = {
         # launchers (reference names, fp32 C)
         "pax_gemm_wmma_launch": (launch7, None),
@@ -78,9 +92,19 @@ def _declare(L: ctypes.CDLL) -> None:
         "pax_gemm_residual_gelu_f16_launch": ([P, P, P, i, i, i, P, P], None),
         "pax_gemm_residual_gelu_erf_f16_launch": ([P, P, P, i, i, i, P, P], None),
         "pax_gemm_ex": ([ctypes.POINTER(GemmDesc), P], i),
+        "pax_gemm_batched_ex": ([ctypes.POINTER(GemmBatchedDesc), P], i),
         "pax_gemm_select_algo": ([ctypes.POINTER(GemmDesc)], i),
         "pax_gemm_pipeline_stages": ([ctypes.POINTER(GemmDesc)], i),
         "pax_gemm_skinny_noalloc": ([ctypes.POINTER(GemmDesc), P], i),
+        # Lean-extraction names (64-bit sizes, pointers as integers)
+        "pax_gemm_wmma_verified": ([u64] * 6, None),
+        "pax_gemm_ptx_verified": ([u64] * 6, None),
+        "pax_gemm_pipeline3_verified": ([u64] * 6, None),
+        "pax_gemm_bias_gelu_verified": ([u64] * 7, None),
+        "pax_gemm_residual_gelu_verified": ([u64] * 7, None),
+        "pax_fp16_add_verified": ([u16] * 2, u16),
+        "pax_fp16_mul_verified": ([u16] * 2, u16),
+        "pax_fp16_fma_verified": ([u16] * 3, u16),
         # bridge
         "pax_validate_buffer": ([buf_p], i),
         "pax_alloc_device_1d": ([sz, sz, P], PaxBuffer),

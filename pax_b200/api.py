@@ -118,6 +118,50 @@ def gemm(A: torch.Tensor, B: torch.Tensor, *, epilogue="none", bias=None, residu
     return out
 
 
+def _batch_view(t: torch.Tensor | None, ndim_item: int, name: str):
+    """(item-0 view, element stride between items) of a batched operand;
+    an operand without the batch dimension is shared (stride 0)."""
+    if t is None:
+        return None, 0
+    if t.dim() == ndim_item:
+        return t, 0
+    if t.dim() != ndim_item + 1:
+        raise ValueError(f"{name} must have {ndim_item} or {ndim_item + 1} dimensions")
+    return t[0], t.stride(0)
+
+
+def gemm_batched(A: torch.Tensor, B: torch.Tensor, *, epilogue="none", bias=None, residual=None,
+                 alpha: float = 1.0, out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16,
+                 algo="auto", stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """C[b] = epilogue(alpha * A[b] @ B[b]) for every batch item b, through
+    pax_gemm_batched_ex.  A is [batch, M, K] or a shared [M, K]; B is
+    [batch, K, N] or a shared [K, N]; bias [batch, N] or [N]; residual
+    [batch, M, N] or [M, N].  C is [batch, M, N]."""
+    nb = max(A.shape[0] if A.dim() == 3 else 1, B.shape[0] if B.dim() == 3 else 1)
+    for t, d, name in ((A, 3, "A"), (B, 3, "B"), (bias, 2, "bias"), (residual, 3, "residual")):
+        if t is not None and t.dim() == d and t.shape[0] != nb:
+            raise ValueError(f"{name} has batch {t.shape[0]}, expected {nb}")
+    A0, sa = _batch_view(A, 2, "A")
+    B0, sb = _batch_view(B, 2, "B")
+    b0, sbias = _batch_view(bias, 1, "bias")
+    r0, sres = _batch_view(residual, 2, "residual")
+    M, N = A0.shape[0], B0.shape[1]
+    if out is None:
+        out = torch.empty((nb, M, N), dtype=out_dtype, device=A.device)
+    if out.dim() != 3 or out.shape[0] != nb:
+        raise ValueError("out must be [batch, M, N]")
+    d = _lib.GemmBatchedDesc()
+    d.gemm = make_desc(A0, B0, out[0], epilogue, b0, r0, alpha, algo)
+    d.batch = nb
+    d.stride_a, d.stride_b, d.stride_c = sa, sb, out.stride(0)
+    d.stride_bias, d.stride_residual = sbias, sres
+    s = stream if stream is not None else torch.cuda.current_stream(A.device)
+    st = _lib.get().pax_gemm_batched_ex(ctypes.byref(d), ctypes.c_void_p(s.cuda_stream))
+    if st != 0:
+        raise PaxError(st, "pax_gemm_batched_ex")
+    return out
+
+
 def select_algo(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, **kw) -> Algo:
     """The algorithm pax_gemm_ex would run (host-only)."""
     d = make_desc(A, B, C, **kw)

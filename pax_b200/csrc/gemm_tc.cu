@@ -56,7 +56,8 @@ static double tc_rounds(long long tiles, long long units) {
 int tc_pick_shape(const Problem& p, int sms) {
     const long long pairs = sms / 2;  // resident pairs are refined at launch (tc_pair_units)
     const long long M = p.M, N = p.N;
-    const long long tm = (M + 127) / 128, tm2 = (M + 255) / 256;
+    // Batch items add tile rows (the model only counts tiles).
+    const long long tm = (M + 127) / 128 * p.batch, tm2 = (M + 255) / 256 * p.batch;
     const double t256 = tc_rounds(tm * ((N + 255) / 256), sms);
     const double t128 = tc_rounds(tm * ((N + 127) / 128), sms) * 0.5 / 0.67;
     const double tpair = tc_rounds(tm2 * ((N + 255) / 256), pairs) / 1.10;
@@ -78,7 +79,7 @@ TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_halves)
     const bool pair = plan.shape == 2 || plan.shape == 4;
     const long long tile_m = pair ? 256 : 128;
     const long long tile_n = plan.shape == 4 ? 512 : plan.shape == 128 ? 128 : 256;
-    const long long tiles = ((p.M + tile_m - 1) / tile_m) * ((p.N + tile_n - 1) / tile_n);
+    const long long tiles = ((p.M + tile_m - 1) / tile_m) * ((p.N + tile_n - 1) / tile_n) * p.batch;
     const long long max_units = pair ? tc_pair_units_f16(dev, sms) : sms;
     // The tail wave: tiles left after whole waves.  When at most half the
     // units would be busy on them, each is cut into two column halves, so

@@ -46,8 +46,30 @@ struct TcParams {
     // (the tail wave) as two column halves each, so
     // num_items = full_items + 2 * tail_tiles.
     int full_items, tail_tiles, num_items;
+    // Batched launch: tiles of item b are [b * batch_tiles, (b + 1) * batch_tiles);
+    // the tensor maps are 3-D with the item as z.  za / zb: whether A / B
+    // have one slice per item (else all items share slice 0).  sbias / sres:
+    // element strides of bias / residual between items.
+    int batch_tiles, za, zb;
+    long long sbias, sres;
     EpiParams epi;
 };
+
+// Output tile -> batch item, and the tile within it.
+__device__ __forceinline__ int tile_batch(int t, const TcParams& p, int& tl) {
+    const int b = t / p.batch_tiles;
+    tl = t - b * p.batch_tiles;
+    return b;
+}
+
+// Epilogue operands of batch item b.
+__device__ __forceinline__ EpiParams epi_for(const TcParams& p, int b, bool res_f32) {
+    EpiParams e = p.epi;
+    if (e.bias) e.bias += (long long)b * p.sbias;
+    if (e.residual)
+        e.residual = static_cast<const char*>(e.residual) + (long long)b * p.sres * (res_f32 ? 4 : 2);
+    return e;
+}
 
 // Work item -> output tile and column half: half = -1 for a whole tile, else
 // 0 / 1 for the left / right BN/2 columns of a tail tile.
@@ -190,8 +212,10 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             for (int item = unit; ok && item < p.num_items; item += units) {
                 int t, half;
                 tc_item(item, p, t, half);
-                int mb, nb;
-                tile_coords(t, p, mb, nb);
+                int tl, mb, nb;
+                const int bz = tile_batch(t, p, tl);
+                const int za = p.za ? bz : 0, zb = p.zb ? bz : 0;
+                tile_coords(tl, p, mb, nb);
                 // The item's columns start at ncol0; this CTA stages `wl` of
                 // them (its half of them in pair mode).
                 const int wl = half < 0 ? Cfg::BN_LOCAL : Cfg::BN_LOCAL / 2;
@@ -212,19 +236,19 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         // the leader announces the bytes of both.
                         const uint32_t fb_leader = mapa_shared(fb, 0);
                         if (leader) mbar_arrive_expect_tx(fb, 2 * bytes);
-                        tma_load_2d_pair(adst, &tmA, fb_leader, kb * Cfg::BK, arow);
+                        tma_load_3d_pair(adst, &tmA, fb_leader, kb * Cfg::BK, arow, za);
                         for (int j = 0; j < wl / 64; ++j) {
                             // Wide tile: boxes 0-1 feed the MMA for item columns
                             // [0, 256), boxes 2-3 the one for [256, 512).
                             const int col = Cfg::WIDE ? ncol0 + (j >> 1) * 256 + (int)rank * 128 + (j & 1) * 64
                                                       : bcol + j * 64;
-                            tma_load_2d_pair(bdst + j * 8192, &tmB, fb_leader, col, kb * Cfg::BK);
+                            tma_load_3d_pair(bdst + j * 8192, &tmB, fb_leader, col, kb * Cfg::BK, zb);
                         }
                     } else {
                         mbar_arrive_expect_tx(fb, bytes);
-                        tma_load_2d(adst, &tmA, fb, kb * Cfg::BK, arow);
+                        tma_load_3d(adst, &tmA, fb, kb * Cfg::BK, arow, za);
                         for (int j = 0; j < wl / 64; ++j)
-                            tma_load_2d(bdst + j * 8192, &tmB, fb, bcol + j * 64, kb * Cfg::BK);
+                            tma_load_3d(bdst + j * 8192, &tmB, fb, bcol + j * 64, kb * Cfg::BK, zb);
                     }
                     issued |= 1u << stage;
                     last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
@@ -331,8 +355,10 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         for (int item = unit; item < p.num_items; item += units) {
             int t, half;
             tc_item(item, p, t, half);
-            int mb, nb;
-            tile_coords(t, p, mb, nb);
+            int tl, mb, nb;
+            const int bz = tile_batch(t, p, tl);
+            tile_coords(tl, p, mb, nb);
+            const EpiParams ep = epi_for(p, bz, RES == 2);
             // This warp's columns of the item: half of them, but at least one
             // 128-byte chunk (an item that narrow leaves the second warp of
             // the lane quarter without columns).
@@ -345,9 +371,9 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             const long long tcol0 = (long long)nb * BN + (half > 0 ? BN / 2 : 0) + wcol;
             // Operands that do not depend on the accumulator are fetched before
             // waiting for it: this warp's bias and the first residual chunk.
-            const uint4 bias8 = bias_tile_load(tcol0, wcols, lane, p.N, p.epi);
+            const uint4 bias8 = bias_tile_load(tcol0, wcols, lane, p.N, ep);
             ResChunk<32, RES> rc;
-            if (wcols > 0) res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, p.epi);
+            if (wcols > 0) res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, ep);
             bool ok = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
@@ -385,11 +411,11 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     tmem_ld_32x32b_x32(t_row + (uint32_t)c, v);
                     tmem_wait_ld();
                     if (ci == nch - 1 && h == EC / 32 - 1) release_accumulator();
-                    epi_linear<32, RES>(v, rc, bias8, c, p.epi);
+                    epi_linear<32, RES>(v, rc, bias8, c, ep);
                     // The residual registers are free again: start the next
                     // sub-chunk's loads, which then overlap the GeLU math below.
                     if constexpr (RES != 0) {
-                        if (c + 32 < nch * EC) res_prefetch<32, RES>(rc, row, tcol0 + c + 32, p.M, p.N, p.epi);
+                        if (c + 32 < nch * EC) res_prefetch<32, RES>(rc, row, tcol0 + c + 32, p.M, p.N, ep);
                     }
                     epi_gelu<32, GELU>(v);
 #pragma unroll
@@ -414,7 +440,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_2d(&tmC, smem_u32(sbuf), (int)(tcol0 + ci * EC), row0);
+                    tma_store_3d(&tmC, smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz);
                     bulk_commit();
                 }
             }
@@ -458,20 +484,31 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// 2-D row-major tensor map: `inner` contiguous elements per row, `outer`
-// rows `pitch` bytes apart, box of box_inner x box_outer, 128B swizzle.
+// 3-D tensor map of `depth` row-major matrices: `inner` contiguous elements
+// per row, `outer` rows `pitch` bytes apart, matrices `zstride` bytes apart;
+// box of box_inner x box_outer x 1, 128B swizzle.
 static bool make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
-                      uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+                      uint64_t depth, uint64_t pitch_bytes, uint64_t zstride_bytes, uint32_t box_inner,
+                      uint32_t box_outer) {
     auto enc = tensor_map_encoder();
     if (!enc) return false;
-    cuuint64_t dims[2] = {inner, outer};
-    cuuint64_t strides[1] = {pitch_bytes};
-    cuuint32_t box[2] = {box_inner, box_outer};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    cuuint64_t dims[3] = {inner, outer, depth};
+    cuuint64_t strides[2] = {pitch_bytes, zstride_bytes};
+    cuuint32_t box[3] = {box_inner, box_outer, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
+}
+
+// Byte stride between batch items for a tensor map: the given element
+// stride, or (single or shared slice) one whole matrix, which is never used
+// to address anything but satisfies the encoder.
+static uint64_t zstride(long long stride_elems, long long rows, long long pitch_bytes, int elem) {
+    if (stride_elems > 0) return (uint64_t)stride_elems * (uint64_t)elem;
+    const uint64_t whole = (uint64_t)rows * (uint64_t)pitch_bytes;
+    return whole > 0 ? ((whole + 15) & ~uint64_t(15)) : 16;
 }
 
 template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
@@ -479,10 +516,17 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     const bool f16 = sizeof(OutT) == 2;
     CUtensorMap tA, tB, tC;
-    if (!make_tmap(&tA, pr.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pr.K, pr.M, pr.lda * 2, 64, 128)) return PAX_ERR_CUDA;
-    if (!make_tmap(&tB, pr.B, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pr.N, pr.K, pr.ldb * 2, 64, 64)) return PAX_ERR_CUDA;
+    const bool za = pr.batch > 1 && pr.sa > 0, zb = pr.batch > 1 && pr.sb > 0;
+    const int ce = f16 ? 2 : 4;
+    if (!make_tmap(&tA, pr.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pr.K, pr.M, za ? pr.batch : 1, pr.lda * 2,
+                   zstride(za ? pr.sa : 0, pr.M, pr.lda * 2, 2), 64, 128))
+        return PAX_ERR_CUDA;
+    if (!make_tmap(&tB, pr.B, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pr.N, pr.K, zb ? pr.batch : 1, pr.ldb * 2,
+                   zstride(zb ? pr.sb : 0, pr.K, pr.ldb * 2, 2), 64, 64))
+        return PAX_ERR_CUDA;
     if (!make_tmap(&tC, pr.C, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pr.N, pr.M,
-                   pr.ldc * (f16 ? 2 : 4), Cfg::EPI_COLS, 32))
+                   pr.batch, pr.ldc * ce, zstride(pr.batch > 1 ? pr.sc : 0, pr.M, pr.ldc * ce, ce), Cfg::EPI_COLS,
+                   32))
         return PAX_ERR_CUDA;
 
     TcParams p;
@@ -491,7 +535,14 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     p.K = (int)pr.K;
     p.tiles_m = (int)((pr.M + Cfg::TILE_M - 1) / Cfg::TILE_M);
     p.tiles_n = (int)((pr.N + BN - 1) / BN);
-    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.batch_tiles = p.tiles_m * p.tiles_n;
+    const long long all_tiles = (long long)p.batch_tiles * pr.batch;
+    if (all_tiles > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
+    p.num_tiles = (int)all_tiles;
+    p.za = za ? 1 : 0;
+    p.zb = zb ? 1 : 0;
+    p.sbias = pr.batch > 1 ? pr.sbias : 0;
+    p.sres = pr.batch > 1 ? pr.sres : 0;
     p.group_m = PAIR ? 8 : 16;
     p.full_items = plan.full_items;
     p.tail_tiles = plan.tail_tiles;

@@ -75,9 +75,26 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 bool tma_compatible(const Problem& p) {
     const long long csz = p.c_f16 ? 2 : 4;
+    // Batch strides address whole matrices through the 3-D tensor maps.
+    const bool batch_ok = p.batch <= 1 || ((p.sa * 2) % 16 == 0 && (p.sb * 2) % 16 == 0 && (p.sc * csz) % 16 == 0 &&
+                                           p.sa < (1LL << 38) && p.sb < (1LL << 38) && p.sc < (1LL << 37));
     return p.K >= 1 && aligned16(p.A) && aligned16(p.B) && aligned16(p.C) && (p.lda * 2) % 16 == 0 &&
            (p.ldb * 2) % 16 == 0 && (p.ldc * csz) % 16 == 0 && p.M < (1LL << 31) && p.N < (1LL << 31) &&
-           p.K < (1LL << 31);
+           p.K < (1LL << 31) && batch_ok;
+}
+
+// Item b of a batched problem as a single problem.
+static Problem batch_item(const Problem& p, long long b) {
+    Problem q = p;
+    q.batch = 1;
+    q.sa = q.sb = q.sc = q.sbias = q.sres = 0;
+    q.A = p.A + b * p.sa;
+    q.B = p.B + b * p.sb;
+    q.C = static_cast<char*>(p.C) + b * p.sc * (p.c_f16 ? 2 : 4);
+    if (p.epi.bias) q.epi.bias = p.epi.bias + b * p.sbias;
+    if (p.epi.residual)
+        q.epi.residual = static_cast<const char*>(p.epi.residual) + b * p.sres * ((p.epi.flags & EPI_RES_F32) ? 4 : 2);
+    return q;
 }
 
 // --------------------------------------------------------- workspaces
@@ -214,7 +231,7 @@ static int env_int(const char* name, int dflt) {
 }
 
 static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
-    if (p.M == 0 || p.N == 0) return PAX_OK;
+    if (p.M == 0 || p.N == 0 || p.batch == 0) return PAX_OK;
     const int dev = current_device();
     const DevInfo di = device_info(dev);
     if (di.major != 10) return fail(PAX_ERR_NO_DEVICE, "device %d is sm_%d%d; this library needs sm_100", dev,
@@ -230,6 +247,15 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
         }
     }
     pax_status_t st;
+    // The tcgen05 kernel takes a whole batch in one launch (3-D tensor
+    // maps); the skinny and CUDA-core kernels run one launch per item.
+    if (p.batch > 1 && (algo == PAX_ALGO_SKINNY || algo == PAX_ALGO_SIMT)) {
+        for (long long b = 0; b < p.batch; ++b) {
+            st = run(batch_item(p, b), algo, s);
+            if (st != PAX_OK) return st;
+        }
+        return set_status(PAX_OK);
+    }
     switch (algo) {
         case PAX_ALGO_TC:
         case PAX_ALGO_TC2: {
@@ -350,6 +376,35 @@ pax_status_t pax_gemm_ex(const pax_gemm_desc_t* desc, cudaStream_t stream) {
     return run(p, desc->algo, stream);
 }
 
+pax_status_t pax_gemm_batched_ex(const pax_gemm_batched_desc_t* desc, cudaStream_t stream) {
+    if (!desc) return fail(PAX_ERR_INVALID, "pax_gemm_batched_ex: NULL descriptor");
+    Problem p;
+    pax_status_t st = normalize(&desc->gemm, &p);
+    if (st != PAX_OK) return st;
+    const long long nb = desc->batch;
+    if (nb < 0 || desc->stride_a < 0 || desc->stride_b < 0 || desc->stride_c < 0 || desc->stride_bias < 0 ||
+        desc->stride_residual < 0)
+        return fail(PAX_ERR_INVALID, "pax_gemm_batched_ex: negative batch or stride");
+    p.batch = nb;
+    if (nb > 1) {
+        p.sa = desc->stride_a;
+        p.sb = desc->stride_b;
+        p.sc = desc->stride_c;
+        p.sbias = desc->stride_bias;
+        p.sres = desc->stride_residual;
+        // Items of C must not overlap: every row of item b ends before item
+        // b + 1 begins.
+        if (p.M > 0 && p.N > 0 && p.sc < (p.M - 1) * p.ldc + p.N)
+            return fail(PAX_ERR_INVALID, "pax_gemm_batched_ex: stride_c %lld overlaps consecutive C items",
+                        (long long)p.sc);
+        // Vector epilogue loads need every item's bias / residual aligned.
+        if ((p.sbias * 2) % 16 != 0) p.epi.flags &= ~EPI_BIAS_VEC;
+        const long long rsz = (p.epi.flags & EPI_RES_F32) ? 4 : 2;
+        if ((p.sres * rsz) % 16 != 0) p.epi.flags &= ~EPI_RES_VEC;
+    }
+    return run(p, desc->gemm.algo, stream);
+}
+
 pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc) {
     Problem p;
     if (normalize(desc, &p) != PAX_OK) return PAX_ALGO_AUTO;
@@ -390,6 +445,53 @@ int pax_gemm_pipeline_stages(const pax_gemm_desc_t* desc) {
         return skinny_stages(p.M, nt);
     }
     return 0;  // CUDA-core kernel: no TMA ring
+}
+
+// ================================================ Lean-extraction symbols
+// pax-lean4/PAX/Extraction.lean:32-56 exports these names with 64-bit sizes
+// and device pointers passed as integers; C is fp32 [M][N], bias fp16 [N],
+// residual fp32 [M][N].  They run the same kernels as pax_gemm_ex on the
+// legacy default stream and report errors as the launchers do.
+static void gemm_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C,
+                          pax_epilogue_t epi, uint64_t extra, const char* who) {
+    if (M > (uint64_t)INT64_MAX || N > (uint64_t)INT64_MAX || K > (uint64_t)INT64_MAX) {
+        fail(PAX_ERR_INVALID, "%s: size above 2^63", who);
+        return;
+    }
+    pax_gemm_desc_t d;
+    memset(&d, 0, sizeof(d));
+    d.A = reinterpret_cast<const void*>((uintptr_t)A);
+    d.B = reinterpret_cast<const void*>((uintptr_t)B);
+    d.C = reinterpret_cast<void*>((uintptr_t)C);
+    d.M = (int64_t)M;
+    d.N = (int64_t)N;
+    d.K = (int64_t)K;
+    d.c_dtype = PAX_DT_F32;
+    d.epilogue = epi;
+    d.alpha = 1.f;
+    if (epi == PAX_EPI_BIAS_GELU_TANH) d.bias = reinterpret_cast<const void*>((uintptr_t)extra);
+    if (epi == PAX_EPI_RESIDUAL_GELU_TANH) d.residual = reinterpret_cast<const void*>((uintptr_t)extra);
+    d.residual_dtype = PAX_DT_F32;
+    d.algo = PAX_ALGO_AUTO;
+    pax_gemm_ex(&d, 0);
+}
+
+void pax_gemm_wmma_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C) {
+    gemm_verified(M, N, K, A, B, C, PAX_EPI_NONE, 0, "pax_gemm_wmma_verified");
+}
+void pax_gemm_ptx_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C) {
+    gemm_verified(M, N, K, A, B, C, PAX_EPI_NONE, 0, "pax_gemm_ptx_verified");
+}
+void pax_gemm_pipeline3_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C) {
+    gemm_verified(M, N, K, A, B, C, PAX_EPI_NONE, 0, "pax_gemm_pipeline3_verified");
+}
+void pax_gemm_bias_gelu_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C,
+                                 uint64_t bias) {
+    gemm_verified(M, N, K, A, B, C, PAX_EPI_BIAS_GELU_TANH, bias, "pax_gemm_bias_gelu_verified");
+}
+void pax_gemm_residual_gelu_verified(uint64_t M, uint64_t N, uint64_t K, uint64_t A, uint64_t B, uint64_t C,
+                                     uint64_t residual) {
+    gemm_verified(M, N, K, A, B, C, PAX_EPI_RESIDUAL_GELU_TANH, residual, "pax_gemm_residual_gelu_verified");
 }
 
 // ======================================================= reference launchers

@@ -20,6 +20,11 @@ struct Problem {
     long long lda, ldb, ldc;
     bool c_f16;
     EpiParams epi;
+    // Batched problems: `batch` independent GEMMs; element strides between
+    // consecutive items of A, B, C, bias and residual (0 = shared by all
+    // items, allowed for A, B, bias and residual).
+    long long batch = 1;
+    long long sa = 0, sb = 0, sc = 0, sbias = 0, sres = 0;
 };
 
 // Per-device facts the launchers need (cached).

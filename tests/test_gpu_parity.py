@@ -433,3 +433,100 @@ def test_wide_tile_epilogues(cuda, rng, monkeypatch, epi, out, shape):
     res = rng.standard_normal((M, N)).astype(np.float16)
     got = run_gemm(A, B, cuda, epi=epi, bias=bias, residual=res, out_dtype=out)
     check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
+
+
+def test_lean_extraction_gemm_symbols(cuda, rng):
+    """pax_gemm_*_verified (pax-lean4/PAX/Extraction.lean:32-56): 64-bit sizes,
+    device pointers as integers, fp32 C, on the legacy default stream."""
+    M, N, K = 320, 264, 200
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    res32 = rng.standard_normal((M, N)).astype(np.float32)
+    tA, tB, tb, tr = to_dev(A, cuda), to_dev(B, cuda), to_dev(bias, cuda), to_dev(res32, cuda)
+    L = pax_b200.lib
+    torch.cuda.synchronize()
+    outs = []
+    for name in ("pax_gemm_wmma_verified", "pax_gemm_ptx_verified", "pax_gemm_pipeline3_verified"):
+        C = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+        torch.cuda.synchronize()
+        getattr(L, name)(M, N, K, tA.data_ptr(), tB.data_ptr(), C.data_ptr())
+        outs.append((C, oracle.gemm(A, B)))
+    C = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    torch.cuda.synchronize()
+    L.pax_gemm_bias_gelu_verified(M, N, K, tA.data_ptr(), tB.data_ptr(), C.data_ptr(), tb.data_ptr())
+    outs.append((C, oracle.gemm(A, B, "bias_gelu_tanh", bias=bias)))
+    C = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    torch.cuda.synchronize()
+    L.pax_gemm_residual_gelu_verified(M, N, K, tA.data_ptr(), tB.data_ptr(), C.data_ptr(), tr.data_ptr())
+    outs.append((C, oracle.gemm(A, B, "residual_gelu_tanh", residual=res32)))
+    torch.cuda.synchronize()
+    assert pax_b200.last_error() == pax_b200.Status.OK
+    for got, ref in outs:
+        check(got.cpu().numpy(), ref, np.float32)
+
+
+# ---------------------------------------------------------------- batched
+def _batched_case(rng, nb, M, N, K, shared_b=False):
+    A = rng.uniform(-1, 1, (nb, M, K)).astype(np.float16)
+    B = rng.uniform(-1, 1, (K, N) if shared_b else (nb, K, N)).astype(np.float16)
+    bias = rng.standard_normal((nb, N)).astype(np.float16)
+    res = rng.standard_normal((nb, M, N)).astype(np.float16)
+    return A, B, bias, res
+
+
+@pytest.mark.parametrize("nb,M,N,K", [(3, 300, 520, 136), (4, 256, 512, 256), (2, 1000, 1480, 328), (5, 16, 1024, 512),
+                                      (3, 40, 136, 72), (2, 17, 33, 31)])
+@pytest.mark.parametrize("epi", ["none", "bias_gelu_tanh", "residual_gelu_erf"])
+@pytest.mark.parametrize("out", [np.float16, np.float32])
+def test_batched_gemm(cuda, rng, nb, M, N, K, epi, out):
+    """pax_gemm_batched_ex: one tcgen05 launch over a 3-D tensor-map batch,
+    or per-item launches for m <= 64 and unaligned shapes; per-item bias and
+    residual."""
+    A, B, bias, res = _batched_case(rng, nb, M, N, K)
+    tA, tB, tb, tr = (to_dev(x, cuda) for x in (A, B, bias, res))
+    td = torch.float16 if out == np.float16 else torch.float32
+    C = pax_b200.gemm_batched(tA, tB, epilogue=epi, bias=tb if "bias" in epi else None,
+                              residual=tr if "residual" in epi else None, out_dtype=td)
+    got = C.cpu().numpy()
+    for b in range(nb):
+        ref = oracle.gemm(A[b], B[b], epi=epi, bias=bias[b], residual=res[b], out_dtype=out)
+        check(got[b], ref, out)
+
+
+def test_batched_shared_weights_and_padded_items(cuda, rng):
+    """B shared by all items (stride 0), A items with padding between them
+    (a slice of a taller tensor), C items with padding too."""
+    nb, M, N, K = 3, 384, 640, 192
+    A_big = rng.uniform(-1, 1, (nb, M + 8, K)).astype(np.float16)
+    A = A_big[:, :M, :]
+    _, B, bias, _ = _batched_case(rng, nb, M, N, K, shared_b=True)
+    tA = to_dev(A_big, cuda)[:, :M, :]
+    tB, tb = to_dev(B, cuda), to_dev(bias[0], cuda)
+    C_big = torch.zeros((nb, M + 16, N), dtype=torch.float16, device=cuda)
+    pax_b200.gemm_batched(tA, tB, epilogue="bias_gelu_tanh", bias=tb, out=C_big[:, :M, :])
+    got = C_big.cpu().numpy()
+    for b in range(nb):
+        check(got[b, :M], oracle.gemm(A[b], B, epi="bias_gelu_tanh", bias=bias[0], out_dtype=np.float16), np.float16)
+        assert not got[b, M:].any()  # padding rows untouched
+
+
+@pytest.mark.parametrize("algo", ["tc2", "wide", "256", "128"])
+def test_batched_bit_exact_every_tile_shape(cuda, rng, monkeypatch, algo):
+    """Integer-valued inputs through each tile shape with batch items that
+    split across waves (and a column-half tail): exact."""
+    algo = _force_tile(monkeypatch, algo)
+    nb, M, N, K = 5, 512, 1040, 256
+    A = rng.integers(-3, 4, (nb, M, K)).astype(np.float16)
+    B = rng.integers(-3, 4, (nb, K, N)).astype(np.float16)
+    C = pax_b200.gemm_batched(to_dev(A, cuda), to_dev(B, cuda), out_dtype=torch.float32, algo=algo)
+    exact = np.einsum("bmk,bkn->bmn", A.astype(np.int64), B.astype(np.int64)).astype(np.float32)
+    assert np.array_equal(C.cpu().numpy(), exact)
+
+
+def test_batched_rejects_overlapping_outputs(cuda):
+    A = torch.zeros((2, 64, 64), dtype=torch.float16, device=cuda)
+    B = torch.zeros((2, 64, 64), dtype=torch.float16, device=cuda)
+    C = torch.zeros((64 * 64 + 64,), dtype=torch.float16, device=cuda)
+    bad = C.as_strided((2, 64, 64), (64, 64, 1))  # item 1 starts one row after item 0
+    with pytest.raises(pax_b200.PaxError):
+        pax_b200.gemm_batched(A, B, out=bad)
