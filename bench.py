@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="pax", choices=["pax", "reference"])
     ap.add_argument("--gather", action="store_true")
+    ap.add_argument("--gather-impl", default="fused", choices=["fused", "nccl"],
+                    help="fused: the GEMM epilogue stores each tile to every peer over NVLink; nccl: all-gather after")
     ap.add_argument("--strong", action="store_true",
                     help="split the configuration's N over the ranks (fixed total work) instead of N per rank")
     ap.add_argument("--seed", type=int, default=0x5EED)
@@ -171,7 +173,9 @@ def workload_config(cfg, world, args):
         "K": cfg["K"],
         "epilogue": cfg["epi"],
         "inputs": cfg["dist"],
-        "parallelism": f"N-split over {world} GPU(s)" + (" + NCCL all-gather of C" if args.gather else ""),
+        "parallelism": f"N-split over {world} GPU(s)" + (
+            "" if not args.gather else " + all-gather of C fused into the GEMM epilogue (TMA stores to peers over NVLink)"
+            if args.gather_impl == "fused" else " + NCCL all-gather of C"),
         "l2": "flushed between steps (256 MiB write, then 256 MiB read of another buffer)",
         "timing": "CUDA events around each launch; all steps queued behind a device sleep (no host gaps)",
     }
@@ -275,7 +279,7 @@ def run_pax(args):
     if args.epilogue:
         cfg["epi"] = args.epilogue
         cfg["name"] += f" [epilogue overridden: {args.epilogue}]"
-    from pax_b200.dist import equal_slabs, gather_columns, slab_bounds
+    from pax_b200.dist import ReplicatedC, equal_slabs, gather_columns, slab_bounds
 
     M, K = cfg["M"], cfg["K"]
     if args.strong:
@@ -316,7 +320,12 @@ def run_pax(args):
     flush = _Flush()
     kw = dict(epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None, residual=res, out=C)
 
+    rc = ReplicatedC(M, n_total, device=dev) if gathered and args.gather_impl == "fused" else None
+
     def step():
+        if rc is not None:
+            rc.gemm_slab(A, B, cfg["epi"], kw["bias"], res)
+            return
         pax_b200.gemm(A, B, **kw)
         if gathered:
             gather_columns(C)
@@ -459,6 +468,8 @@ def run_pax(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        if rc is not None:
+            rc.close()
         dist.destroy_process_group()
     return 0
 

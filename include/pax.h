@@ -222,6 +222,31 @@ typedef struct {
 } pax_gemm_batched_desc_t;
 pax_status_t pax_gemm_batched_ex(const pax_gemm_batched_desc_t* desc, cudaStream_t stream);
 
+/* Replicated output (new; the multi-GPU north star's "all-gather of C only
+ * when the caller asks for a replicated output"): pax_gemm_ex, and the same
+ * kernel also stores every finished tile of C to each of `n_replicas`
+ * (0..7) further buffers of C's shape and pitch, typically the same region
+ * of other GPUs' C buffers mapped with pax_ipc_import.  The copies travel
+ * over NVLink while the kernel computes later tiles.  Each replica receives
+ * complete, system-visible data once the kernel has finished; a reader on
+ * another GPU must order its reads after that (for example, by a collective
+ * on the same streams).  Tensor-core path only (m > 64, 16-byte aligned
+ * rows): other problems return PAX_ERR_UNSUPPORTED. */
+pax_status_t pax_gemm_replicated_ex(const pax_gemm_desc_t* desc, void* const* replicas, int n_replicas,
+                                   cudaStream_t stream);
+
+/* CUDA IPC handle of the allocation holding a device pointer, plus the
+ * pointer's offset in it (new).  pax_ipc_import maps it in another process
+ * (peer access enabled lazily) and returns the same address there;
+ * pax_ipc_close unmaps. */
+typedef struct {
+    unsigned char handle[64];
+    uint64_t offset;
+} pax_ipc_handle_t;
+pax_status_t pax_ipc_export(const void* device_ptr, pax_ipc_handle_t* out);
+pax_status_t pax_ipc_import(const pax_ipc_handle_t* handle, void** device_ptr);
+pax_status_t pax_ipc_close(void* device_ptr);
+
 /* The algorithm pax_gemm_ex would run for desc with algo = PAX_ALGO_AUTO (new;
  * host-only, launches nothing). */
 pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc);

@@ -51,6 +51,11 @@ class GemmDesc(ctypes.Structure):
     ]
 
 
+class IpcHandle(ctypes.Structure):
+    """pax_ipc_handle_t (include/pax.h)."""
+    _fields_ = [("handle", ctypes.c_ubyte * 64), ("offset", ctypes.c_uint64)]
+
+
 class GemmBatchedDesc(ctypes.Structure):
     """pax_gemm_batched_desc_t (include/pax.h)."""
     _fields_ = [
@@ -93,6 +98,10 @@ def _declare(L: ctypes.CDLL) -> None:
         "pax_gemm_residual_gelu_erf_f16_launch": ([P, P, P, i, i, i, P, P], None),
         "pax_gemm_ex": ([ctypes.POINTER(GemmDesc), P], i),
         "pax_gemm_batched_ex": ([ctypes.POINTER(GemmBatchedDesc), P], i),
+        "pax_gemm_replicated_ex": ([ctypes.POINTER(GemmDesc), ctypes.POINTER(P), i, P], i),
+        "pax_ipc_export": ([P, ctypes.POINTER(IpcHandle)], i),
+        "pax_ipc_import": ([ctypes.POINTER(IpcHandle), ctypes.POINTER(P)], i),
+        "pax_ipc_close": ([P], i),
         "pax_gemm_select_algo": ([ctypes.POINTER(GemmDesc)], i),
         "pax_gemm_pipeline_stages": ([ctypes.POINTER(GemmDesc)], i),
         "pax_gemm_skinny_noalloc": ([ctypes.POINTER(GemmDesc), P], i),

@@ -101,17 +101,26 @@ def make_desc(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, epilogue="none"
 
 def gemm(A: torch.Tensor, B: torch.Tensor, *, epilogue="none", bias=None, residual=None, alpha: float = 1.0,
          out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16, algo="auto",
-         stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+         stream: torch.cuda.Stream | None = None, replicas: list[int] | None = None) -> torch.Tensor:
     """C = epilogue(alpha * A @ B) on the current (or given) CUDA stream.
 
     A [M, K] and B [K, N] are float16 row-major CUDA tensors; C is float16 or
     float32.  epilogue is one of none, bias, bias_gelu_tanh, bias_gelu_erf,
     residual_gelu_tanh, residual_gelu_erf, gelu_tanh, gelu_erf, residual.
+    replicas: device addresses of further buffers with out's shape and pitch
+    (usually other GPUs' memory, see pax_b200.dist.ReplicatedC) that the same
+    kernel also writes C to.
     """
     if out is None:
         out = torch.empty((A.shape[0], B.shape[1]), dtype=out_dtype, device=A.device)
     d = make_desc(A, B, out, epilogue, bias, residual, alpha, algo)
     s = stream if stream is not None else torch.cuda.current_stream(A.device)
+    if replicas:
+        arr = (ctypes.c_void_p * len(replicas))(*replicas)
+        st = _lib.get().pax_gemm_replicated_ex(ctypes.byref(d), arr, len(replicas), ctypes.c_void_p(s.cuda_stream))
+        if st != 0:
+            raise PaxError(st, "pax_gemm_replicated_ex")
+        return out
     st = _lib.get().pax_gemm_ex(ctypes.byref(d), ctypes.c_void_p(s.cuda_stream))
     if st != 0:
         raise PaxError(st, "pax_gemm_ex")
@@ -173,6 +182,31 @@ def pipeline_stages(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, **kw) -> 
     the CUDA-core kernel)."""
     d = make_desc(A, B, C, **kw)
     return int(_lib.get().pax_gemm_pipeline_stages(ctypes.byref(d)))
+
+
+def ipc_export(t: torch.Tensor) -> bytes:
+    """CUDA IPC handle (72 bytes) of the memory at t.data_ptr()."""
+    h = _lib.IpcHandle()
+    st = _lib.get().pax_ipc_export(ctypes.c_void_p(t.data_ptr()), ctypes.byref(h))
+    if st != 0:
+        raise PaxError(st, "pax_ipc_export")
+    return bytes(h)
+
+
+def ipc_import(handle: bytes) -> int:
+    """Map another process's exported device memory; returns its address here."""
+    h = _lib.IpcHandle.from_buffer_copy(handle)
+    ptr = ctypes.c_void_p()
+    st = _lib.get().pax_ipc_import(ctypes.byref(h), ctypes.byref(ptr))
+    if st != 0:
+        raise PaxError(st, "pax_ipc_import")
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    st = _lib.get().pax_ipc_close(ctypes.c_void_p(ptr))
+    if st != 0:
+        raise PaxError(st, "pax_ipc_close")
 
 
 def device_error() -> Status:

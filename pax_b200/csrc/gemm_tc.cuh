@@ -33,6 +33,7 @@
 
 #include <cudaTypedefs.h>
 #include <stdlib.h>
+#include <string.h>
 #include <mutex>
 #include <stdio.h>
 
@@ -53,6 +54,17 @@ struct TcParams {
     int batch_tiles, za, zb;
     long long sbias, sres;
     EpiParams epi;
+};
+
+// Extra destinations of C (replicated output): tensor maps with C's shape
+// and pitch over other buffers, typically other GPUs' memory mapped into
+// this process.  Every finished chunk of C is stored to each of them too, so
+// an all-gather of C happens inside the epilogue, overlapped with the MMAs of
+// the next tiles.  Stores only: no TMA load ever reads another GPU here.
+constexpr int kTcMaxReplicas = 7;
+struct TcReplicas {
+    CUtensorMap map[kTcMaxReplicas];
+    int n;
 };
 
 // Output tile -> batch item, and the tile within it.
@@ -142,7 +154,8 @@ __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& mb, i
 template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
 __global__ void __launch_bounds__(64 + 32 * 8, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, const TcParams p) {
+                   const __grid_constant__ CUtensorMap tmC, const TcParams p,
+                   const __grid_constant__ TcReplicas reps) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem =
@@ -441,6 +454,8 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                 __syncwarp();
                 if (lane == 0) {
                     tma_store_3d(&tmC, smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz);
+                    for (int d = 0; d < reps.n; ++d)
+                        tma_store_3d(&reps.map[d], smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz);
                     bulk_commit();
                 }
             }
@@ -449,7 +464,12 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                 acc_phase ^= 1u;
             }
         }
-        if (lane == 0) bulk_wait<0>();
+        if (lane == 0) {
+            bulk_wait<0>();
+            // Stores to other GPUs are complete; make them visible system-wide
+            // before the grid ends.
+            if (reps.n > 0) __threadfence_system();
+        }
         __syncwarp();
     }
 
@@ -528,6 +548,15 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
                    pr.batch, pr.ldc * ce, zstride(pr.batch > 1 ? pr.sc : 0, pr.M, pr.ldc * ce, ce), Cfg::EPI_COLS,
                    32))
         return PAX_ERR_CUDA;
+    TcReplicas reps;
+    memset(&reps, 0, sizeof(reps));
+    if (pr.n_replicas < 0 || pr.n_replicas > kTcMaxReplicas) return PAX_ERR_INVALID;
+    reps.n = pr.n_replicas;
+    for (int d = 0; d < reps.n; ++d)
+        if (!make_tmap(&reps.map[d], pr.replicas[d], f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                       pr.N, pr.M, pr.batch, pr.ldc * ce, zstride(pr.batch > 1 ? pr.sc : 0, pr.M, pr.ldc * ce, ce),
+                       Cfg::EPI_COLS, 32))
+            return PAX_ERR_CUDA;
 
     TcParams p;
     p.M = (int)pr.M;
@@ -567,9 +596,9 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         cfg.gridDim = dim3(2 * plan.units);
-        if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p) != cudaSuccess) return PAX_ERR_CUDA;
+        if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
     } else {
-        kern<<<plan.units, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(tA, tB, tC, p);
+        kern<<<plan.units, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(tA, tB, tC, p, reps);
     }
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }

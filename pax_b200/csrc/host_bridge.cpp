@@ -16,7 +16,9 @@
 #include <string.h>
 
 #include <map>
+#include <cuda.h>
 #include <mutex>
+#include <vector>
 #include <utility>
 
 #include "../../include/pax.h"
@@ -249,6 +251,9 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
     pax_status_t st;
     // The tcgen05 kernel takes a whole batch in one launch (3-D tensor
     // maps); the skinny and CUDA-core kernels run one launch per item.
+    if (p.n_replicas > 0 && algo != PAX_ALGO_TC && algo != PAX_ALGO_TC2)
+        return fail(PAX_ERR_UNSUPPORTED, "replicated output needs the tensor-core path (m > %lld, 16-byte aligned rows)",
+                    kSkinnyMaxM);
     if (p.batch > 1 && (algo == PAX_ALGO_SKINNY || algo == PAX_ALGO_SIMT)) {
         for (long long b = 0; b < p.batch; ++b) {
             st = run(batch_item(p, b), algo, s);
@@ -374,6 +379,94 @@ pax_status_t pax_gemm_ex(const pax_gemm_desc_t* desc, cudaStream_t stream) {
     pax_status_t st = normalize(desc, &p);
     if (st != PAX_OK) return st;
     return run(p, desc->algo, stream);
+}
+
+pax_status_t pax_gemm_replicated_ex(const pax_gemm_desc_t* desc, void* const* replicas, int n_replicas,
+                                   cudaStream_t stream) {
+    Problem p;
+    pax_status_t st = normalize(desc, &p);
+    if (st != PAX_OK) return st;
+    if (n_replicas < 0 || n_replicas > 7 || (n_replicas > 0 && !replicas))
+        return fail(PAX_ERR_INVALID, "pax_gemm_replicated_ex: %d replicas (0..7 allowed)", n_replicas);
+    for (int i = 0; i < n_replicas; ++i)
+        if (!replicas[i] || !aligned16(replicas[i]))
+            return fail(PAX_ERR_INVALID, "pax_gemm_replicated_ex: replica %d is NULL or not 16-byte aligned", i);
+    p.replicas = replicas;
+    p.n_replicas = n_replicas;
+    return run(p, desc->algo, stream);
+}
+
+// ------------------------------------------------------------- CUDA IPC
+// Handles that let each rank map the others' C buffers for
+// pax_gemm_replicated_ex.  A handle names the whole allocation that holds
+// the pointer plus the pointer's offset in it, so buffers carved out of a
+// larger allocation (a framework's caching allocator) can be shared.
+static std::mutex g_ipc_mu;
+static std::vector<std::pair<void*, void*>> g_ipc_open;  // (pointer returned, mapped base)
+
+static CUresult mem_range(CUdeviceptr* base, size_t* size, CUdeviceptr ptr) {
+    using Fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &f, 3020, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(f);
+    });
+    return fn ? fn(base, size, ptr) : CUDA_ERROR_NOT_SUPPORTED;
+}
+
+pax_status_t pax_ipc_export(const void* device_ptr, pax_ipc_handle_t* out) {
+    if (!device_ptr || !out) return fail(PAX_ERR_INVALID, "pax_ipc_export: NULL argument");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (mem_range(&base, &size, (CUdeviceptr)(uintptr_t)device_ptr) != CUDA_SUCCESS)
+        return fail(PAX_ERR_CUDA, "pax_ipc_export: pointer is not device memory of this process");
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>((uintptr_t)base)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PAX_ERR_CUDA, "pax_ipc_export: cudaIpcGetMemHandle failed");
+    }
+    static_assert(sizeof(h) == sizeof(out->handle), "IPC handle size");
+    memcpy(out->handle, &h, sizeof(h));
+    out->offset = (uint64_t)((uintptr_t)device_ptr - (uintptr_t)base);
+    return set_status(PAX_OK);
+}
+
+pax_status_t pax_ipc_import(const pax_ipc_handle_t* handle, void** device_ptr) {
+    if (!handle || !device_ptr) return fail(PAX_ERR_INVALID, "pax_ipc_import: NULL argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle->handle, sizeof(h));
+    void* base = nullptr;
+    if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PAX_ERR_CUDA, "pax_ipc_import: cudaIpcOpenMemHandle failed");
+    }
+    *device_ptr = static_cast<char*>(base) + handle->offset;
+    std::lock_guard<std::mutex> lk(g_ipc_mu);
+    g_ipc_open.emplace_back(*device_ptr, base);
+    return set_status(PAX_OK);
+}
+
+pax_status_t pax_ipc_close(void* device_ptr) {
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_ipc_mu);
+        for (size_t i = 0; i < g_ipc_open.size(); ++i)
+            if (g_ipc_open[i].first == device_ptr) {
+                base = g_ipc_open[i].second;
+                g_ipc_open.erase(g_ipc_open.begin() + (long)i);
+                break;
+            }
+    }
+    if (!base) return fail(PAX_ERR_INVALID, "pax_ipc_close: pointer was not imported");
+    if (cudaIpcCloseMemHandle(base) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PAX_ERR_CUDA, "pax_ipc_close: cudaIpcCloseMemHandle failed");
+    }
+    return set_status(PAX_OK);
 }
 
 pax_status_t pax_gemm_batched_ex(const pax_gemm_batched_desc_t* desc, cudaStream_t stream) {

@@ -25,6 +25,10 @@ struct Problem {
     // items, allowed for A, B, bias and residual).
     long long batch = 1;
     long long sa = 0, sb = 0, sc = 0, sbias = 0, sres = 0;
+    // Replicated output: C is also stored, by the same kernel, to these
+    // buffers (same shape and pitch; usually peer GPUs' memory).
+    void* const* replicas = nullptr;
+    int n_replicas = 0;
 };
 
 // Per-device facts the launchers need (cached).

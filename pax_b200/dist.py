@@ -3,9 +3,11 @@
 The product C = epi(A . B) has independent output columns, so P ranks split
 B, bias and C along N: rank p owns columns [p*Ns, (p+1)*Ns), holds all of A
 and computes its slab with the single-GPU kernels, with no communication.
-When the caller wants C replicated on every rank, `gather_columns` runs one
-NCCL all-gather of the contiguous slabs into a [P][M][Ns] staging buffer and
-packs it into row-major M x N.  The reference has no multi-GPU code; this is
+When the caller wants C replicated on every rank, `ReplicatedC` fuses the
+all-gather into the GEMM: each rank's kernel also stores its tiles straight
+into the peers' C over NVLink.  `gather_columns` is the unfused baseline:
+one NCCL all-gather of the contiguous slabs into a [P][M][Ns] staging buffer,
+packed into row-major M x N.  The reference has no multi-GPU code; this is
 the partitioning BASELINE's configuration 5 asks for.
 """
 from __future__ import annotations
@@ -61,3 +63,73 @@ def gather_columns(C_slab: torch.Tensor, group=None) -> torch.Tensor:
     staging = C_slab.new_empty((world * M, Ns))  # rank-major stack of slabs
     dist.all_gather_into_tensor(staging, C_slab.contiguous(), group=group)
     return staging.view(world, M, Ns).permute(1, 0, 2).reshape(M, world * Ns)
+
+
+class ReplicatedC:
+    """C [M, N_total] replicated on every rank, filled by one fused kernel per
+    rank instead of a GEMM followed by an all-gather.
+
+    Every rank allocates the full C and maps the other ranks' C buffers
+    (CUDA IPC, pax_ipc_export / pax_ipc_import).  `gemm` computes this rank's
+    column slab with pax_gemm_replicated_ex: the epilogue stores each finished
+    tile into the local C and, over NVLink, into the same place of every
+    peer's C while the kernel goes on with later tiles.  Stores only: no
+    kernel reads another GPU's memory.
+
+    Ordering: a one-element all-reduce before the kernel (every rank has
+    finished reading the previous contents) and one after it (every rank's
+    slab has landed everywhere) bracket each call, on the current stream.
+
+    `_export`, `_import`, `_close` and `gemm_fn` exist so that the host logic
+    can be tested without GPUs.
+    """
+
+    def __init__(self, M: int, N_total: int, dtype: torch.dtype = torch.float16, device=None, group=None, *,
+                 _export: Callable | None = None, _import: Callable | None = None, _close: Callable | None = None):
+        from . import api
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not equal_slabs(N_total, self.world):
+            raise ValueError("replicated C needs N_total divisible by 8 * ranks")
+        self.full = torch.empty((M, N_total), dtype=dtype, device=device)
+        self._close = _close or api.ipc_close
+        mine = (_export or api.ipc_export)(self.full)
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, mine, group=group)
+        imp = _import or api.ipc_import
+        self.peers = {r: imp(h) for r, h in enumerate(handles) if r != self.rank}
+        self.slab = slab_bounds(N_total, self.world, self.rank)
+        self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+
+    def replica_addresses(self) -> list[int]:
+        """Where this rank's slab goes in every peer's C (same offset as here)."""
+        off = self.slab[0] * self.full.element_size()
+        return [base + off for _, base in sorted(self.peers.items())]
+
+    def gemm(self, A: torch.Tensor, B: torch.Tensor, epilogue: str = "none", bias: torch.Tensor | None = None,
+             residual: torch.Tensor | None = None, gemm_fn: Callable | None = None) -> torch.Tensor:
+        """full = epi(A . B) on every rank, from the full-width B (and bias /
+        residual); this rank computes its column slab."""
+        s, e = self.slab
+        return self.gemm_slab(A, B[:, s:e], epilogue, bias[s:e] if bias is not None else None,
+                              residual[:, s:e] if residual is not None else None, gemm_fn)
+
+    def gemm_slab(self, A: torch.Tensor, B_slab: torch.Tensor, epilogue: str = "none",
+                  bias_slab: torch.Tensor | None = None, residual_slab: torch.Tensor | None = None,
+                  gemm_fn: Callable | None = None) -> torch.Tensor:
+        """As `gemm`, from this rank's slabs of B, bias and residual only."""
+        if gemm_fn is None:
+            from .api import gemm as gemm_fn
+        s, e = self.slab
+        dist.all_reduce(self._flag, group=self.group)
+        gemm_fn(A, B_slab, epilogue=epilogue, bias=bias_slab, residual=residual_slab, out=self.full[:, s:e],
+                replicas=self.replica_addresses())
+        dist.all_reduce(self._flag, group=self.group)
+        return self.full
+
+    def close(self) -> None:
+        for ptr in self.peers.values():
+            self._close(ptr)
+        self.peers = {}

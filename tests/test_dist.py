@@ -91,3 +91,67 @@ def test_split_and_gather_equal_single_rank(world):
     bias = torch.randn((N,), generator=g).half()
     full = oracle.gemm(A.numpy(), B.numpy(), epi="bias_gelu_tanh", bias=bias.numpy(), out_dtype=np.float16)
     assert np.array_equal(C.view(np.uint16), full.view(np.uint16))
+
+
+def _replicated_worker(rank, world, port, M, N, K, q):
+    """ReplicatedC host logic with stand-ins for the IPC calls and the kernel:
+    each rank's kernel call must get its own column slab as `out` and, as
+    replicas, every peer's base address plus that slab's byte offset."""
+    from pax_b200.dist import ReplicatedC
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        fake_base = lambda r: (r + 1) << 40  # noqa: E731
+        calls = []
+
+        def fake_gemm(A, B, *, epilogue, bias, residual, out, replicas):
+            calls.append((B.shape, out.data_ptr() - rc.full.data_ptr(), out.shape, out.stride(), list(replicas)))
+            out.copy_(_oracle_gemm(A, B, epilogue=epilogue, bias=bias, residual=residual))
+
+        rc = ReplicatedC(M, N, device="cpu", _export=lambda t: str(dist.get_rank()).encode(),
+                         _import=lambda h: fake_base(int(h.decode())), _close=lambda p: None)
+        g = torch.Generator().manual_seed(7)
+        A = (torch.rand((M, K), generator=g) * 2 - 1).half()
+        B = (torch.rand((K, N), generator=g) * 2 - 1).half()
+        bias = torch.randn((N,), generator=g).half()
+        rc.gemm(A, B, "bias_gelu_tanh", bias=bias, gemm_fn=fake_gemm)
+        rc.close()
+        q.put((rank, calls, sorted(rc.peers.items()), rc.slab))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_replicated_c_host_logic(world):
+    M, N, K = 16, 32 * world, 24
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_replicated_worker, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    deadline = time.time() + 180
+    while len(got) < world and time.time() < deadline:
+        try:
+            r, calls, peers, slab = q.get(timeout=1)
+            got[r] = (calls, peers, slab)
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in procs):
+                break
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert len(got) == world, f"ranks failed: {[p.exitcode for p in procs]}"
+    Ns = N // world
+    for r, (calls, peers, slab) in got.items():
+        assert slab == (r * Ns, (r + 1) * Ns)
+        assert peers == []  # closed
+        (bshape, out_off, out_shape, out_stride, replicas), = calls
+        assert tuple(bshape) == (K, Ns)
+        assert out_off == r * Ns * 2 and tuple(out_shape) == (M, Ns) and out_stride == (N, 1)  # bytes
+        expect = [((p + 1) << 40) + r * Ns * 2 for p in range(world) if p != r]
+        assert replicas == expect

@@ -27,7 +27,7 @@ def _rank(rank, world, port, M, N, K, q):
     from datetime import timedelta
 
     import pax_b200
-    from pax_b200.dist import gather_columns, local_slab_gemm
+    from pax_b200.dist import ReplicatedC, gather_columns, local_slab_gemm
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -40,8 +40,15 @@ def _rank(rank, world, port, M, N, K, q):
         bias = torch.randn((N,), generator=g).half()
         C_slab = local_slab_gemm(A.to(dev), B.to(dev), rank, world, epilogue="bias_gelu_tanh", bias=bias.to(dev))
         C = gather_columns(C_slab)
+        # Fused: each rank's kernel also stores its slab into the peer's C.
+        rc = ReplicatedC(M, N, device=dev)
+        fused = []
+        for _ in range(2):  # the second call overwrites the same buffers
+            rc.full.zero_()
+            fused.append(rc.gemm(A.to(dev), B.to(dev), "bias_gelu_tanh", bias=bias.to(dev)).cpu().numpy())
         torch.cuda.synchronize()
-        q.put((rank, C.cpu().numpy(), int(pax_b200.device_error())))
+        rc.close()
+        q.put((rank, C.cpu().numpy(), int(pax_b200.device_error()), fused))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -62,8 +69,8 @@ def test_two_gpu_slabs_and_gather(cuda):
     deadline = time.time() + 240
     while len(got) < world and time.time() < deadline:
         try:
-            r, C, err = q.get(timeout=1)
-            got[r] = (C, err)
+            r, C, err, fused = q.get(timeout=1)
+            got[r] = (C, err, fused)
         except queue.Empty:
             if any(p.exitcode not in (None, 0) for p in procs):
                 break
@@ -77,7 +84,9 @@ def test_two_gpu_slabs_and_gather(cuda):
     B = (torch.rand((K, N), generator=g) * 2 - 1).half().numpy()
     bias = torch.randn((N,), generator=g).half().numpy()
     ref = oracle.gemm(A, B, epi="bias_gelu_tanh", bias=bias, out_dtype=np.float16)
-    for r, (C, err) in got.items():
+    for r, (C, err, fused) in got.items():
         assert err == 0
         assert oracle.normwise_error(C, ref) <= 2e-3
+        for F in fused:  # the fused all-gather delivers the same bits as NCCL
+            assert np.array_equal(F.view(np.uint16), C.view(np.uint16))
     assert np.array_equal(got[0][0].view(np.uint16), got[1][0].view(np.uint16))
