@@ -530,3 +530,35 @@ def test_batched_rejects_overlapping_outputs(cuda):
     bad = C.as_strided((2, 64, 64), (64, 64, 1))  # item 1 starts one row after item 0
     with pytest.raises(pax_b200.PaxError):
         pax_b200.gemm_batched(A, B, out=bad)
+
+
+@pytest.mark.parametrize("algo", ["tc2", "wide", "256", "128"])
+@pytest.mark.parametrize("out", [np.float16, np.float32])
+def test_replicated_output_to_local_buffers(cuda, rng, monkeypatch, algo, out):
+    """pax_gemm_replicated_ex with replicas in this GPU's memory: every
+    replica, with the same pitch as C (here a column slab of a wider buffer),
+    holds exactly C; the bytes around the slab are untouched."""
+    algo = _force_tile(monkeypatch, algo)
+    M, N, K, W = 640, 520, 136, 1040
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    td = torch.float16 if out == np.float16 else torch.float32
+    full = [torch.zeros((M, W), dtype=td, device=cuda) for _ in range(4)]
+    C = full[0][:, 8:8 + N]
+    reps = [f[:, 8:8 + N].data_ptr() for f in full[1:]]
+    pax_b200.gemm(to_dev(A, cuda), to_dev(B, cuda), epilogue="bias_gelu_tanh", bias=to_dev(bias, cuda), out=C,
+                  algo=algo, replicas=reps)
+    ref = oracle.gemm(A, B, epi="bias_gelu_tanh", bias=bias, out_dtype=out)
+    got = [f.cpu().numpy() for f in full]
+    check(got[0][:, 8:8 + N], ref, out)
+    for g in got[1:]:
+        assert np.array_equal(g, got[0])
+
+
+def test_replicated_output_rejects_skinny(cuda):
+    A = torch.zeros((16, 256), dtype=torch.float16, device=cuda)
+    B = torch.zeros((256, 512), dtype=torch.float16, device=cuda)
+    C = torch.zeros((16, 512), dtype=torch.float16, device=cuda)
+    R = torch.zeros((16, 512), dtype=torch.float16, device=cuda)
+    with pytest.raises(pax_b200.PaxError):
+        pax_b200.gemm(A, B, out=C, replicas=[R.data_ptr()])
