@@ -261,6 +261,46 @@ def traffic_from_profiles(config: int):
     return None
 
 
+def decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev, layers: int = 8, reps: int = 20):
+    """The decode case the skinny kernel is for: `layers` M=16 GEMMs back to
+    back, each with its own weights (together 8 x 134 MB, far above L2, so
+    every launch streams its B from HBM).  Consecutive launches overlap
+    through programmatic dependent launch: a launch's prologue and first B
+    prefetches run during the previous launch's tail.  Timed per chain with
+    CUDA events (L2 flushed before each chain); reported per GEMM."""
+    import torch
+
+    import pax_b200
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(0xDEC0)
+    Bs = [(torch.randn((K, N), generator=g, device=dev) * 0.02).half() for _ in range(layers)]
+    Cs = [torch.empty((A.shape[0], N), dtype=torch.float16, device=dev) for _ in range(layers)]
+    kw = dict(epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None)
+
+    def chain():
+        for B, C in zip(Bs, Cs):
+            pax_b200.gemm(A, B, out=C, **kw)
+
+    for _ in range(3):
+        flush.zero_()
+        chain()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    torch.cuda._sleep(int(0.02 * 2.0e9))
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        chain()
+        e1.record()
+    torch.cuda.synchronize()
+    per = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev) / layers
+    gbs = alg_bytes / (per * 1e-3) / 1e9
+    del Bs, Cs
+    return {"launches_per_chain": layers, "us_per_gemm": per * 1e3, "achieved": gbs, "frac": gbs / hbm,
+            "pdl": os.environ.get("PAX_PDL", "1") != "0"}
+
+
 def run_pax(args):
     import numpy as np  # noqa: F401
     import torch
@@ -431,7 +471,8 @@ def run_pax(args):
             roofline = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                         "traffic": traffic_from_profiles(args.config),
                         "peak_kind": f"{peak_kind} (copy bandwidth)", "algorithmic_bytes_per_launch": alg_bytes,
-                        "tflops": achieved, "best_launch_ms": kernel_ms}
+                        "tflops": achieved, "best_launch_ms": kernel_ms,
+                        "stream": decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev)}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, dt, rows, threads, kind, _ = cpu_gemm_sample(cfg, args.cpu_seconds, args.seed)

@@ -181,6 +181,9 @@ __global__ void __launch_bounds__(192, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // A following kernel launched with programmatic serialization may start
+    // its prologue now; it waits for this grid before touching memory.
+    if (threadIdx.x == 0) pdl_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -190,6 +193,22 @@ __global__ void __launch_bounds__(192, 1)
             bool ok = true;
             long long cur = sk_cursor0(p);
             SkSeg sg;
+            {
+                // Before waiting for the previous grid: pull this CTA's first
+                // k-blocks of B into L2.  A prefetch only warms the cache, so
+                // it cannot observe data that grid is still writing; every
+                // load into shared memory happens after the wait.
+                long long c0 = cur;
+                SkSeg s0;
+                if (sk_next_seg(p, c0, s0)) {
+                    const int n0 = s0.nk < STAGES ? s0.nk : STAGES;
+                    for (int j = 0; j < n0; ++j)
+#pragma unroll
+                        for (int b = 0; b < NT / 64; ++b)
+                            tma_prefetch_l2(&tmB, s0.tile * NT + b * 64, (s0.kb0 + j * s0.kstep) * 64);
+                }
+            }
+            pdl_wait();
             while (ok && sk_next_seg(p, cur, sg))
             for (int j = 0; j < sg.nk; ++j) {
                 const int tile = sg.tile;
@@ -267,6 +286,7 @@ __global__ void __launch_bounds__(192, 1)
             mbar_wait(drain_bar, 0, nullptr);
         }
     } else {
+        pdl_wait();  // bias, residual, C and the workspace may belong to the previous grid
         const int q = warp & 3;
         const int et = threadIdx.x - 64;  // 0..127 among epilogue threads
         const int n_local = q * 32 + lane;
@@ -489,7 +509,17 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
     auto kern = gemm_skinny_kernel<MP, NT>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES) != cudaSuccess)
         return PAX_ERR_CUDA;
-    kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(tA, tB, p);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, p) != cudaSuccess) return PAX_ERR_CUDA;
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }
 

@@ -214,10 +214,14 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int num_kb = (p.K + Cfg::BK - 1) / Cfg::BK;
+    // A following kernel launched with programmatic serialization may start
+    // its prologue now; it waits for this grid before touching memory.
+    if (threadIdx.x == 0) pdl_launch_dependents();
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
+            pdl_wait();  // A and B may be written by the previous grid
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -359,6 +363,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         }
     } else {
         // ------------------------------------------------ epilogue warps
+        pdl_wait();  // bias, residual and C may belong to the previous grid
         constexpr int EC = Cfg::EPI_COLS;
         const int q = warp & 3;          // TMEM lane quarter this warp may read
         const int wh = (warp - 2) >> 2;  // which half of the item's columns
@@ -583,23 +588,21 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     // Attribute is per device; setting it again is cheap and idempotent.
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES) != cudaSuccess)
         return PAX_ERR_CUDA;
-    if constexpr (PAIR) {
-        cudaLaunchConfig_t cfg = {};
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.blockDim = dim3(Cfg::THREADS);
-        cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-        cfg.stream = stream;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        cfg.gridDim = dim3(2 * plan.units);
-        if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
-    } else {
-        kern<<<plan.units, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(tA, tB, tC, p, reps);
-    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = PAIR ? 2 : 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(Cfg::THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = PAIR ? 2 : 1;
+    cfg.gridDim = dim3(PAIR ? 2 * plan.units : plan.units);
+    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }
 

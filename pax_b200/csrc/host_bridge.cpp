@@ -232,6 +232,11 @@ static int env_int(const char* name, int dflt) {
     return v ? atoi(v) : dflt;
 }
 
+bool pdl_enabled() {
+    static const bool on = env_int("PAX_PDL", 1) != 0;
+    return on;
+}
+
 static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
     if (p.M == 0 || p.N == 0 || p.batch == 0) return PAX_OK;
     const int dev = current_device();

@@ -68,6 +68,10 @@ void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int
 pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, int* counters, cudaStream_t stream,
                               int slices = 0, bool korder = false);
 
+// Launch the GEMM kernels with programmatic stream serialization, so that a
+// kernel's prologue overlaps the previous kernel in the stream (default on;
+// PAX_PDL=0 turns it off).
+bool pdl_enabled();
 // Shared-memory pipeline depth (TMA ring stages) of each kernel variant.
 int tc_stages(int shape);
 int skinny_stages(long long M, int nt);

@@ -163,6 +163,23 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
         "r"(src), "r"(x), "r"(y), "r"(z)
         : "memory");
 }
+// L2 prefetch of one 2-D box (a hint: no data reaches the SM).
+__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+
+// Programmatic dependent launch.  pdl_wait: block until the grid this one
+// depends on (the previous kernel in the stream, when launched with
+// programmatic stream serialization) has completed and its memory is
+// visible; a no-op otherwise.  pdl_launch_dependents: allow the next such
+// grid to be scheduled now (it waits in its own pdl_wait before touching
+// memory this grid writes).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void bulk_wait_read() {
