@@ -577,7 +577,13 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     p.zb = zb ? 1 : 0;
     p.sbias = pr.batch > 1 ? pr.sbias : 0;
     p.sres = pr.batch > 1 ? pr.sres : 0;
-    p.group_m = PAIR ? 8 : 16;
+    // Tiles run in column-major groups of group_m tile rows.  Per k-step the
+    // U tiles in flight fetch group_m A slices and U / group_m B slices, so
+    // the DRAM traffic of large-K problems is least near
+    // sqrt(U * tile_n / tile_m): 8 for 256 x 256 pair tiles (U = 74), 16
+    // measured best for 256 x 512 (C5: 1182 vs 1049 TF/s with 8) and for
+    // 128-row one-CTA tiles (U = 148).
+    p.group_m = (PAIR && !Cfg::WIDE) ? 8 : 16;
     p.full_items = plan.full_items;
     p.tail_tiles = plan.tail_tiles;
     p.num_items = plan.full_items + 2 * plan.tail_tiles;
