@@ -562,3 +562,54 @@ def test_replicated_output_rejects_skinny(cuda):
     R = torch.zeros((16, 512), dtype=torch.float16, device=cuda)
     with pytest.raises(pax_b200.PaxError):
         pax_b200.gemm(A, B, out=C, replicas=[R.data_ptr()])
+
+
+# ------------------------------------------------ chained launches (PDL)
+@pytest.mark.parametrize("m1,m2", [(512, 768), (16, 16), (512, 16), (16, 1024)])
+def test_back_to_back_dependent_gemms(cuda, rng, m1, m2):
+    """Kernels launched with programmatic dependent launch start their
+    prologue while the previous kernel runs.  A chain where each GEMM reads
+    the previous one's output (RAW), then overwrites a buffer the previous
+    one read (WAR), queued without synchronisation, must match the oracle
+    run step by step.  Shapes mix the skinny and tcgen05 kernels."""
+    K0, N1, N2 = 256, 512, 384
+    A0 = rng.uniform(-1, 1, (m1, K0)).astype(np.float16)
+    B1 = (rng.uniform(-1, 1, (K0, N1)) / 8).astype(np.float16)
+    B2 = (rng.uniform(-1, 1, (N1, N2)) / 8).astype(np.float16)
+    B3 = (rng.uniform(-1, 1, (K0, N1)) / 8).astype(np.float16)
+    tA0, tB1, tB2, tB3 = (to_dev(x, cuda) for x in (A0, B1, B2, B3))
+    C1 = torch.empty((m1, N1), dtype=torch.float16, device=cuda)
+    for _ in range(3):
+        torch.cuda.synchronize()
+        pax_b200.gemm(tA0, tB1, out=C1)                     # C1 = A0 B1
+        C2 = pax_b200.gemm(C1[:m2] if m2 <= m1 else C1.repeat(1, 1)[:m2], tB2)  # reads C1 (RAW)
+        pax_b200.gemm(tA0, tB3, out=C1)                     # overwrites C1 after C2 read it (WAR)
+        torch.cuda.synchronize()
+        ref1 = oracle.gemm(A0, B1, out_dtype=np.float16)
+        ref2 = oracle.gemm(ref1[:m2], B2, out_dtype=np.float16)
+        ref3 = oracle.gemm(A0, B3, out_dtype=np.float16)
+        check(C2.cpu().numpy(), ref2, np.float16)
+        check(C1.cpu().numpy(), ref3, np.float16)
+
+
+def test_long_dependent_chain(cuda, rng):
+    """Twelve GEMMs, each consuming the previous output, alternating the
+    skinny (m = 16) and tcgen05 (m = 384) kernels through a residual."""
+    N = 256
+    Bs = [(rng.uniform(-1, 1, (N, N)) / 16).astype(np.float16) for _ in range(12)]
+    X0 = rng.uniform(-1, 1, (384, N)).astype(np.float16)
+    tB = [to_dev(b, cuda) for b in Bs]
+    X = to_dev(X0, cuda)
+    ref = X0
+    torch.cuda.synchronize()
+    for i in range(12):
+        rows = 16 if i % 2 else 384
+        Y = pax_b200.gemm(X[:rows], tB[i], epilogue="residual_gelu_tanh", residual=X[:rows])
+        ref_y = oracle.gemm(ref[:rows], Bs[i], epi="residual_gelu_tanh", residual=ref[:rows], out_dtype=np.float16)
+        if rows == 384:
+            X, ref = Y, ref_y
+        else:
+            X = torch.cat([Y, X[16:]])
+            ref = np.concatenate([ref_y, ref[16:]])
+    torch.cuda.synchronize()
+    check(X.cpu().numpy(), ref, np.float16)
