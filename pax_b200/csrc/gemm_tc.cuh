@@ -133,8 +133,6 @@ struct TcCfg {
     static constexpr uint32_t NUM_BARS = 2 * STAGES + 5;
     static constexpr size_t SMEM_BYTES =
         1024 + (size_t)STAGES * STAGE_BYTES + STG_TOTAL + NUM_BARS * 8 + 16;
-    static constexpr uint32_t IDESC = umma_idesc_f16(PAIR ? 256 : 128, MMA_N, /*a_mn*/ false, /*b_mn*/ true);
-    static constexpr uint32_t IDESC_HALF = umma_idesc_f16(PAIR ? 256 : 128, WIDE ? 256 : BN / 2, false, true);
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
     static_assert((BN_LOCAL / 2) % 64 == 0, "B (and a half of it) is staged in 64-column boxes");
@@ -151,11 +149,40 @@ __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& mb, i
     nb = r / gm;
 }
 
+// One unit of work: output rows [mb * TILE_M, +TILE_M) of batch item bz,
+// columns [col0, col0 + w).  w is the tile width, half of it (tail halves),
+// or, from a planned table, 512 / 384 / 256 / 128 for CTA-pair tiles.
+struct TcWork {
+    int bz, mb, col0, w;
+};
+
+template <int BN>
+__device__ __forceinline__ TcWork tc_work(int k, const TcParams& p, const TcItemTable& tab) {
+    TcWork w;
+    if (tab.count > 0) {
+        const unsigned int it = tab.item[k];
+        const int code = (int)(it >> 28) & 3;
+        w.bz = 0;
+        w.mb = (int)(it & 0xFFFFu);
+        w.col0 = (int)((it >> 16) & 0xFFFu) * 128;
+        w.w = code == 0 ? 512 : code == 1 ? 384 : code == 2 ? 256 : 128;
+    } else {
+        int t, half, tl, nb;
+        tc_item(k, p, t, half);
+        w.bz = tile_batch(t, p, tl);
+        tile_coords(tl, p, w.mb, nb);
+        w.col0 = nb * BN + (half > 0 ? BN / 2 : 0);
+        w.w = half < 0 ? BN : BN / 2;
+    }
+    return w;
+}
+
+
 template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
 __global__ void __launch_bounds__(64 + 32 * 8, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const TcParams p,
-                   const __grid_constant__ TcReplicas reps) {
+                   const __grid_constant__ TcReplicas reps, const __grid_constant__ TcItemTable tab) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem =
@@ -181,6 +208,11 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
     const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     const bool leader = rank == 0;
+    // This unit's work items: a planned table's slice, or round-robin.
+    const bool tabbed = tab.count > 0;
+    const int k_begin = tabbed ? tab.unit_start[unit] : unit;
+    const int k_end = tabbed ? tab.unit_start[unit + 1] : p.num_items;
+    const int k_step = tabbed ? 1 : units;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -226,20 +258,17 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             uint32_t phase = 0;
             bool ok = true;
             uint32_t issued = 0, last_parity = 0;
-            for (int item = unit; ok && item < p.num_items; item += units) {
-                int t, half;
-                tc_item(item, p, t, half);
-                int tl, mb, nb;
-                const int bz = tile_batch(t, p, tl);
-                const int za = p.za ? bz : 0, zb = p.zb ? bz : 0;
-                tile_coords(tl, p, mb, nb);
-                // The item's columns start at ncol0; this CTA stages `wl` of
-                // them (its half of them in pair mode).
-                const int wl = half < 0 ? Cfg::BN_LOCAL : Cfg::BN_LOCAL / 2;
-                const int ncol0 = nb * BN + (half > 0 ? BN / 2 : 0);
-                const int arow = mb * Cfg::TILE_M + (int)rank * Cfg::BM;
-                const int bcol = ncol0 + (int)rank * wl;
-                const uint32_t bytes = Cfg::A_BYTES + (uint32_t)wl * Cfg::BK * 2;
+            for (int k = k_begin; ok && k < k_end; k += k_step) {
+                const TcWork wk = tc_work<BN>(k, p, tab);
+                const int za = p.za ? wk.bz : 0, zb = p.zb ? wk.bz : 0;
+                // MMA 0 covers item columns [0, n0), MMA 1 (items wider than
+                // 256 only) [n0, w).  This CTA stages l0 / l1 of each: half of
+                // them in pair mode (CTA r the r-th half), all of them alone.
+                const int n0 = wk.w < 256 ? wk.w : 256, n1 = wk.w - n0;
+                const int l0 = PAIR ? n0 / 2 : n0, l1 = PAIR ? n1 / 2 : n1;
+                const int c0 = wk.col0 + (int)rank * l0, c1 = wk.col0 + n0 + (int)rank * l1;
+                const int arow = wk.mb * Cfg::TILE_M + (int)rank * Cfg::BM;
+                const uint32_t bytes = Cfg::A_BYTES + (uint32_t)(l0 + l1) * Cfg::BK * 2;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
                         ok = false;
@@ -254,18 +283,19 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         const uint32_t fb_leader = mapa_shared(fb, 0);
                         if (leader) mbar_arrive_expect_tx(fb, 2 * bytes);
                         tma_load_3d_pair(adst, &tmA, fb_leader, kb * Cfg::BK, arow, za);
-                        for (int j = 0; j < wl / 64; ++j) {
-                            // Wide tile: boxes 0-1 feed the MMA for item columns
-                            // [0, 256), boxes 2-3 the one for [256, 512).
-                            const int col = Cfg::WIDE ? ncol0 + (j >> 1) * 256 + (int)rank * 128 + (j & 1) * 64
-                                                      : bcol + j * 64;
-                            tma_load_3d_pair(bdst + j * 8192, &tmB, fb_leader, col, kb * Cfg::BK, zb);
-                        }
+                        // 64-column boxes: MMA 0's first, then MMA 1's.
+                        for (int j = 0; j < l0 / 64; ++j)
+                            tma_load_3d_pair(bdst + j * 8192, &tmB, fb_leader, c0 + j * 64, kb * Cfg::BK, zb);
+                        for (int j = 0; j < l1 / 64; ++j)
+                            tma_load_3d_pair(bdst + (l0 / 64 + j) * 8192, &tmB, fb_leader, c1 + j * 64, kb * Cfg::BK,
+                                             zb);
                     } else {
                         mbar_arrive_expect_tx(fb, bytes);
                         tma_load_3d(adst, &tmA, fb, kb * Cfg::BK, arow, za);
-                        for (int j = 0; j < wl / 64; ++j)
-                            tma_load_3d(bdst + j * 8192, &tmB, fb, bcol + j * 64, kb * Cfg::BK, zb);
+                        for (int j = 0; j < l0 / 64; ++j)
+                            tma_load_3d(bdst + j * 8192, &tmB, fb, c0 + j * 64, kb * Cfg::BK, zb);
+                        for (int j = 0; j < l1 / 64; ++j)
+                            tma_load_3d(bdst + (l0 / 64 + j) * 8192, &tmB, fb, c1 + j * 64, kb * Cfg::BK, zb);
                     }
                     issued |= 1u << stage;
                     last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
@@ -300,15 +330,18 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             // only in the start-address field (address >> 4 in the low bits).
             const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA), 16, 1024);
             const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB), 8192, 1024);
-            for (int item = unit; ok && item < p.num_items; item += units) {
-                int t, half;
-                tc_item(item, p, t, half);
-                const uint32_t idesc = half < 0 ? Cfg::IDESC : Cfg::IDESC_HALF;
+            for (int k = k_begin; ok && k < k_end; k += k_step) {
+                const TcWork wk = tc_work<BN>(k, p, tab);
+                // MMA 0: item columns [0, n0); MMA 1 (items wider than 256):
+                // [n0, w), its B boxes after MMA 0's in the stage.
+                const int n0 = wk.w < 256 ? wk.w : 256, n1 = wk.w - n0;
+                const uint32_t id0 = umma_idesc_f16(PAIR ? 256 : 128, n0, false, true);
+                const uint32_t id1 = umma_idesc_f16(PAIR ? 256 : 128, n1 > 0 ? n1 : 16, false, true);
+                const uint64_t b1 = (uint64_t)((((PAIR ? n0 / 2 : n0) / 64) * 8192) >> 4);
                 // In pair mode the releases come from both CTAs' epilogues.
                 if (!mbar_wait<PAIR>(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-                const bool two = Cfg::WIDE && half < 0;  // wide whole tile: two N = 256 MMAs per k-step
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(full0 + 8u * stage, phase, abort_flag)) {
                         ok = false;
@@ -321,13 +354,13 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
                         const uint64_t ad = as + (uint64_t)((kk * 32) >> 4);    // +32 B along K
                         const uint64_t bd = bs + (uint64_t)((kk * 2048) >> 4);  // +16 rows of K
+                        const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
                         if constexpr (PAIR) {
-                            tc_mma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
-                            if (two)
-                                tc_mma_f16_pair(d_tmem + 256u, ad, bd + (uint64_t)((2 * 8192) >> 4), idesc,
-                                                (kb | kk) != 0 ? 1u : 0u);
+                            tc_mma_f16_pair(d_tmem, ad, bd, id0, accum);
+                            if (n1 > 0) tc_mma_f16_pair(d_tmem + (uint32_t)n0, ad, bd + b1, id1, accum);
                         } else {
-                            tc_mma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+                            tc_mma_f16(d_tmem, ad, bd, id0, accum);
+                            if (n1 > 0) tc_mma_f16(d_tmem + (uint32_t)n0, ad, bd + b1, id1, accum);
                         }
                     }
                     if constexpr (PAIR) {
@@ -370,23 +403,20 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         uint8_t* sbuf = sStg + (warp - 2) * Cfg::STG_BYTES;
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int item = unit; item < p.num_items; item += units) {
-            int t, half;
-            tc_item(item, p, t, half);
-            int tl, mb, nb;
-            const int bz = tile_batch(t, p, tl);
-            tile_coords(tl, p, mb, nb);
+        for (int k = k_begin; k < k_end; k += k_step) {
+            const TcWork wk = tc_work<BN>(k, p, tab);
+            const int bz = wk.bz, mb = wk.mb;
             const EpiParams ep = epi_for(p, bz, RES == 2);
             // This warp's columns of the item: half of them, but at least one
             // 128-byte chunk (an item that narrow leaves the second warp of
             // the lane quarter without columns).
-            const int width = half < 0 ? BN : BN / 2;
+            const int width = wk.w;
             const bool two = width / 2 >= EC;
             const int wcols = two ? width / 2 : (wh == 0 ? width : 0);
             const int wcol = two ? wh * (width / 2) : 0;  // offset within the item
             const int row0 = mb * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
             const long long row = (long long)row0 + lane;
-            const long long tcol0 = (long long)nb * BN + (half > 0 ? BN / 2 : 0) + wcol;
+            const long long tcol0 = (long long)wk.col0 + wcol;
             // Operands that do not depend on the accumulator are fetched before
             // waiting for it: this warp's bias and the first residual chunk.
             const uint4 bias8 = bias_tile_load(tcol0, wcols, lane, p.N, ep);
@@ -539,6 +569,9 @@ static uint64_t zstride(long long stride_elems, long long rows, long long pitch_
 template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
 static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaStream_t stream) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
+    static const TcItemTable kNoTable{};  // count 0: the kernel's own schedule
+    const TcItemTable* tab = plan.table ? plan.table : &kNoTable;
+    if (plan.table && (!Cfg::WIDE || plan.table->count <= 0 || pr.batch != 1)) return PAX_ERR_INVALID;
     const bool f16 = sizeof(OutT) == 2;
     CUtensorMap tA, tB, tC;
     const bool za = pr.batch > 1 && pr.sa > 0, zb = pr.batch > 1 && pr.sb > 0;
@@ -608,7 +641,7 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     cfg.attrs = attr;
     cfg.numAttrs = PAIR ? 2 : 1;
     cfg.gridDim = dim3(PAIR ? 2 * plan.units : plan.units);
-    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
+    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p, reps, *tab) != cudaSuccess) return PAX_ERR_CUDA;
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }
 

@@ -49,6 +49,9 @@ struct TcPlan {
     int units = 0;
     int full_items = 0;
     int tail_tiles = 0;
+    // Wide tile only: a host-planned per-unit list of mixed-width items
+    // (null: the kernel's round-robin schedule of whole tiles and halves).
+    const TcItemTable* table = nullptr;
 };
 TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_halves);
 pax_status_t launch_tc(const Problem& p, const TcPlan& plan, cudaStream_t stream);

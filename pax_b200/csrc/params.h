@@ -25,4 +25,17 @@ struct EpiParams {
     int flags;
 };
 
+// Host-planned work list of the tcgen05 kernel: the items of unit u (a CTA
+// or CTA pair) are item[unit_start[u] .. unit_start[u + 1]).  An item packs
+// its 256-row block (bits 0-15), its first column / 128 (bits 16-27) and its
+// width code (bits 28-29: 512, 384, 256, 128 columns).  count = 0: no table,
+// the kernel's own round-robin schedule.
+struct TcItemTable {
+    static constexpr int kMaxUnits = 160;
+    static constexpr int kMaxItems = 640;
+    int count;
+    int unit_start[kMaxUnits + 1];
+    unsigned int item[kMaxItems];
+};
+
 }  // namespace pax
