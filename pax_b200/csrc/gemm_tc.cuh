@@ -53,6 +53,10 @@ struct TcParams {
     // element strides of bias / residual between items.
     int batch_tiles, za, zb;
     long long sbias, sres;
+    // Planned work list (device memory): plan[0 .. units] are the units'
+    // first items, plan[units + 1 + k] item k (TcItemTable's packing).
+    // Null: round-robin over num_items.
+    const int* plan;
     EpiParams epi;
 };
 
@@ -157,10 +161,10 @@ struct TcWork {
 };
 
 template <int BN>
-__device__ __forceinline__ TcWork tc_work(int k, const TcParams& p, const TcItemTable& tab) {
+__device__ __forceinline__ TcWork tc_work(int k, const TcParams& p, const unsigned int* items) {
     TcWork w;
-    if (tab.count > 0) {
-        const unsigned int it = tab.item[k];
+    if (items != nullptr) {
+        const unsigned int it = __ldg(items + k);
         const int code = (int)(it >> 28) & 3;
         w.bz = 0;
         w.mb = (int)(it & 0xFFFFu);
@@ -182,7 +186,7 @@ template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
 __global__ void __launch_bounds__(64 + 32 * 8, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const TcParams p,
-                   const __grid_constant__ TcReplicas reps, const __grid_constant__ TcItemTable tab) {
+                   const __grid_constant__ TcReplicas reps) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem =
@@ -209,10 +213,11 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     const bool leader = rank == 0;
     // This unit's work items: a planned table's slice, or round-robin.
-    const bool tabbed = tab.count > 0;
-    const int k_begin = tabbed ? tab.unit_start[unit] : unit;
-    const int k_end = tabbed ? tab.unit_start[unit + 1] : p.num_items;
+    const bool tabbed = p.plan != nullptr;
+    const int k_begin = tabbed ? __ldg(p.plan + unit) : unit;
+    const int k_end = tabbed ? __ldg(p.plan + unit + 1) : p.num_items;
     const int k_step = tabbed ? 1 : units;
+    const unsigned int* items = tabbed ? reinterpret_cast<const unsigned int*>(p.plan + units + 1) : nullptr;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -259,12 +264,12 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             bool ok = true;
             uint32_t issued = 0, last_parity = 0;
             for (int k = k_begin; ok && k < k_end; k += k_step) {
-                const TcWork wk = tc_work<BN>(k, p, tab);
+                const TcWork wk = tc_work<BN>(k, p, items);
                 const int za = p.za ? wk.bz : 0, zb = p.zb ? wk.bz : 0;
                 // MMA 0 covers item columns [0, n0), MMA 1 (items wider than
                 // 256 only) [n0, w).  This CTA stages l0 / l1 of each: half of
                 // them in pair mode (CTA r the r-th half), all of them alone.
-                const int n0 = wk.w < 256 ? wk.w : 256, n1 = wk.w - n0;
+                const int n0 = wk.w < 256 ? wk.w : 256, n1 = Cfg::WIDE ? wk.w - n0 : 0;
                 const int l0 = PAIR ? n0 / 2 : n0, l1 = PAIR ? n1 / 2 : n1;
                 const int c0 = wk.col0 + (int)rank * l0, c1 = wk.col0 + n0 + (int)rank * l1;
                 const int arow = wk.mb * Cfg::TILE_M + (int)rank * Cfg::BM;
@@ -331,10 +336,12 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA), 16, 1024);
             const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB), 8192, 1024);
             for (int k = k_begin; ok && k < k_end; k += k_step) {
-                const TcWork wk = tc_work<BN>(k, p, tab);
+                const TcWork wk = tc_work<BN>(k, p, items);
                 // MMA 0: item columns [0, n0); MMA 1 (items wider than 256):
                 // [n0, w), its B boxes after MMA 0's in the stage.
-                const int n0 = wk.w < 256 ? wk.w : 256, n1 = wk.w - n0;
+                // Only wide-tile items have a second MMA: a compile-time zero
+                // elsewhere keeps the MMA issue loop free of branches.
+                const int n0 = wk.w < 256 ? wk.w : 256, n1 = Cfg::WIDE ? wk.w - n0 : 0;
                 const uint32_t id0 = umma_idesc_f16(PAIR ? 256 : 128, n0, false, true);
                 const uint32_t id1 = umma_idesc_f16(PAIR ? 256 : 128, n1 > 0 ? n1 : 16, false, true);
                 const uint64_t b1 = (uint64_t)((((PAIR ? n0 / 2 : n0) / 64) * 8192) >> 4);
@@ -350,17 +357,32 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     tc_fence_after();
                     const uint64_t as = adesc0 + (uint64_t)((stage * Cfg::A_BYTES) >> 4);
                     const uint64_t bs = bdesc0 + (uint64_t)((stage * Cfg::B_BYTES) >> 4);
+                    // Straight-line MMA sequences: the one- or two-MMA choice is
+                    // made once per stage, not between MMAs.
+                    if (n1 > 0) {
 #pragma unroll
-                    for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
-                        const uint64_t ad = as + (uint64_t)((kk * 32) >> 4);    // +32 B along K
-                        const uint64_t bd = bs + (uint64_t)((kk * 2048) >> 4);  // +16 rows of K
-                        const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
-                        if constexpr (PAIR) {
-                            tc_mma_f16_pair(d_tmem, ad, bd, id0, accum);
-                            if (n1 > 0) tc_mma_f16_pair(d_tmem + (uint32_t)n0, ad, bd + b1, id1, accum);
-                        } else {
-                            tc_mma_f16(d_tmem, ad, bd, id0, accum);
-                            if (n1 > 0) tc_mma_f16(d_tmem + (uint32_t)n0, ad, bd + b1, id1, accum);
+                        for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
+                            const uint64_t ad = as + (uint64_t)((kk * 32) >> 4);    // +32 B along K
+                            const uint64_t bd = bs + (uint64_t)((kk * 2048) >> 4);  // +16 rows of K
+                            const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
+                            if constexpr (PAIR) {
+                                tc_mma_f16_pair(d_tmem, ad, bd, id0, accum);
+                                tc_mma_f16_pair(d_tmem + (uint32_t)n0, ad, bd + b1, id1, accum);
+                            } else {
+                                tc_mma_f16(d_tmem, ad, bd, id0, accum);
+                                tc_mma_f16(d_tmem + (uint32_t)n0, ad, bd + b1, id1, accum);
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
+                            const uint64_t ad = as + (uint64_t)((kk * 32) >> 4);
+                            const uint64_t bd = bs + (uint64_t)((kk * 2048) >> 4);
+                            const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
+                            if constexpr (PAIR)
+                                tc_mma_f16_pair(d_tmem, ad, bd, id0, accum);
+                            else
+                                tc_mma_f16(d_tmem, ad, bd, id0, accum);
                         }
                     }
                     if constexpr (PAIR) {
@@ -404,7 +426,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int k = k_begin; k < k_end; k += k_step) {
-            const TcWork wk = tc_work<BN>(k, p, tab);
+            const TcWork wk = tc_work<BN>(k, p, items);
             const int bz = wk.bz, mb = wk.mb;
             const EpiParams ep = epi_for(p, bz, RES == 2);
             // This warp's columns of the item: half of them, but at least one
@@ -569,9 +591,8 @@ static uint64_t zstride(long long stride_elems, long long rows, long long pitch_
 template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
 static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaStream_t stream) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
-    static const TcItemTable kNoTable{};  // count 0: the kernel's own schedule
-    const TcItemTable* tab = plan.table ? plan.table : &kNoTable;
-    if (plan.table && (!Cfg::WIDE || plan.table->count <= 0 || pr.batch != 1)) return PAX_ERR_INVALID;
+    if (plan.table && (!Cfg::WIDE || !plan.table_dev || plan.table->count <= 0 || pr.batch != 1))
+        return PAX_ERR_INVALID;
     const bool f16 = sizeof(OutT) == 2;
     CUtensorMap tA, tB, tC;
     const bool za = pr.batch > 1 && pr.sa > 0, zb = pr.batch > 1 && pr.sb > 0;
@@ -610,6 +631,7 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     p.zb = zb ? 1 : 0;
     p.sbias = pr.batch > 1 ? pr.sbias : 0;
     p.sres = pr.batch > 1 ? pr.sres : 0;
+    p.plan = plan.table ? plan.table_dev : nullptr;
     // Tiles run in column-major groups of group_m tile rows.  Per k-step the
     // U tiles in flight fetch group_m A slices and U / group_m B slices, so
     // the DRAM traffic of large-K problems is least near
@@ -641,7 +663,7 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     cfg.attrs = attr;
     cfg.numAttrs = PAIR ? 2 : 1;
     cfg.gridDim = dim3(PAIR ? 2 * plan.units : plan.units);
-    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p, reps, *tab) != cudaSuccess) return PAX_ERR_CUDA;
+    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }
 

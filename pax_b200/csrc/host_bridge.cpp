@@ -237,6 +237,8 @@ bool pdl_enabled() {
     return on;
 }
 
+bool tc_planning_enabled() { return env_int("PAX_TC_PLAN", 1) != 0; }
+
 static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
     if (p.M == 0 || p.N == 0 || p.batch == 0) return PAX_OK;
     const int dev = current_device();
@@ -278,7 +280,7 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
             }
             // The tail wave's tiles run as column halves (PAX_TC_HALVES=0
             // turns that off for comparisons).
-            const TcPlan plan = tc_plan(p, shape, dev, di.sms, env_int("PAX_TC_HALVES", 1) != 0);
+            const TcPlan plan = tc_plan(p, shape, dev, di.sms, env_int("PAX_TC_HALVES", 1) != 0, s);
             st = launch_tc(p, plan, s);
             break;
         }

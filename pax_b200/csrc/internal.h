@@ -52,8 +52,9 @@ struct TcPlan {
     // Wide tile only: a host-planned per-unit list of mixed-width items
     // (null: the kernel's round-robin schedule of whole tiles and halves).
     const TcItemTable* table = nullptr;
+    const int* table_dev = nullptr;  // its device copy (current device)
 };
-TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_halves);
+TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_halves, cudaStream_t stream);
 pax_status_t launch_tc(const Problem& p, const TcPlan& plan, cudaStream_t stream);
 pax_status_t launch_simt(const Problem& p, cudaStream_t stream);
 // Skinny kernel, nt (128, 256 or 512) output columns per work unit: `ws`
@@ -75,6 +76,9 @@ pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, int
 // kernel's prologue overlaps the previous kernel in the stream (default on;
 // PAX_PDL=0 turns it off).
 bool pdl_enabled();
+// Planned mixed-width tiling for the wide shape (default on; PAX_TC_PLAN=0
+// turns it off).
+bool tc_planning_enabled();
 // Shared-memory pipeline depth (TMA ring stages) of each kernel variant.
 int tc_stages(int shape);
 int skinny_stages(long long M, int nt);

@@ -29,7 +29,8 @@ struct EpiParams {
 // or CTA pair) are item[unit_start[u] .. unit_start[u + 1]).  An item packs
 // its 256-row block (bits 0-15), its first column / 128 (bits 16-27) and its
 // width code (bits 28-29: 512, 384, 256, 128 columns).  count = 0: no table,
-// the kernel's own round-robin schedule.
+// the kernel's own round-robin schedule.  The kernel reads a device copy
+// (unit_start then item, as ints) through TcParams::plan.
 struct TcItemTable {
     static constexpr int kMaxUnits = 160;
     static constexpr int kMaxItems = 640;

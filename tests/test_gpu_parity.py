@@ -613,3 +613,32 @@ def test_long_dependent_chain(cuda, rng):
             ref = np.concatenate([ref_y, ref[16:]])
     torch.cuda.synchronize()
     check(X.cpu().numpy(), ref, np.float16)
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 512), (4736, 4096, 256), (3000, 5000, 128), (1000, 1480, 328),
+                                   (2304, 2560, 200), (520, 8200, 64)])
+def test_planned_wide_tiling_bit_exact(cuda, rng, monkeypatch, M, N, K):
+    """Wide tiles re-planned as mixed 512 / 384 / 256-column items (the
+    host's per-pair work table): integer-valued inputs give exact results,
+    identical to the round-robin schedule (PAX_TC_PLAN=0), ragged edges
+    included."""
+    monkeypatch.setenv("PAX_TC_SHAPE", "4")
+    A = rng.integers(-3, 4, (M, K)).astype(np.float16)
+    B = rng.integers(-3, 4, (K, N)).astype(np.float16)
+    exact = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.float32)
+    planned = run_gemm(A, B, cuda, out_dtype=np.float32)
+    assert np.array_equal(planned, exact)
+    monkeypatch.setenv("PAX_TC_PLAN", "0")
+    assert np.array_equal(run_gemm(A, B, cuda, out_dtype=np.float32), planned)
+
+
+@pytest.mark.parametrize("epi", ["bias_gelu_tanh", "residual_gelu_erf"])
+@pytest.mark.parametrize("out", [np.float16, np.float32])
+def test_planned_wide_tiling_epilogues(cuda, rng, monkeypatch, epi, out):
+    monkeypatch.setenv("PAX_TC_SHAPE", "4")
+    M, N, K = 3000, 5000, 128
+    A, B = inputs(rng, M, N, K)
+    bias = rng.standard_normal(N).astype(np.float16)
+    res = rng.standard_normal((M, N)).astype(np.float16)
+    got = run_gemm(A, B, cuda, epi=epi, bias=bias, residual=res, out_dtype=out)
+    check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
