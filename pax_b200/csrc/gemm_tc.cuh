@@ -1,4 +1,4 @@
-// gemm_tc.cu -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
+// gemm_tc.cuh -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
 //
 //   C[M][N] = epi(A[M][K] . B[K][N]),  A, B fp16 row-major, fp32 accumulate in
 //   TMEM, C fp32 or fp16 row-major.
@@ -8,20 +8,26 @@
 // src/rtx_gemm_epilogue.cu:243-356); the epilogue semantics are those of
 // src/rtx_gemm_epilogue.cu:176-233 (see epilogue.cuh).
 //
-// CTA layout (320 threads, one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: A tile 128x64 (K-major) and B tile 64xBN
-//               (N-major) per k-block into a STAGES-deep ring of
+// CTA layout (320 threads, one CTA per SM, or one CTA pair per two SMs with
+// tcgen05 cta_group::2; persistent over work items):
+//   warp 0      TMA producer: A 128x64 (K-major) and the item's B columns
+//               64 at a time (N-major) per k-block into a STAGES-deep ring of
 //               128B-swizzled shared-memory slots, mbarrier full/empty pairs.
-//   warp 1      MMA issuer: allocates TMEM (2 accumulators of 128 lanes x BN
-//               fp32 columns), issues tcgen05.mma M=128 N=BN K=16 (four per
-//               k-block), commits slot releases and accumulator-ready.
+//   warp 1      MMA issuer (the pair leader): tcgen05.mma K=16, four k-steps
+//               per stage, one MMA of N <= 256 per k-step (two for items
+//               wider than 256 columns, sharing A); commits slot releases
+//               and accumulator-ready.
 //   warps 2..9  epilogue, two per TMEM lane quarter, each on half of the
-//               tile's columns: tcgen05.ld 32 lanes x 32 columns, bias /
+//               item's columns: tcgen05.ld 32 lanes x 32 columns, bias /
 //               residual / GeLU in registers, fp32->fp16, swizzled staging
-//               in shared memory, TMA store.  Accumulator i is handed back to
-//               the MMA warp as soon as it is read, so the epilogue of tile t
-//               overlaps the main loop of tile t+1.
-// Ragged M/N/K edges: TMA zero-fills out-of-range loads and clips stores.
+//               in shared memory, TMA store (and, for replicated outputs, one
+//               more TMA store per replica).  With two accumulators, buffer i
+//               is handed back to the MMA warp as soon as it is read, so the
+//               epilogue of one item overlaps the main loop of the next.
+// Work items: whole tiles and column halves of the tail wave in round-robin
+// order, or (wide tiles) a host-planned per-pair list of 512 / 384 / 256
+// column items.  Ragged M/N/K edges: TMA zero-fills out-of-range loads and
+// clips stores.
 //
 // This header holds the kernel template and its launcher template; the
 // gemm_tc_f16.cu / gemm_tc_f32.cu translation units instantiate them per
@@ -116,7 +122,6 @@ template <int BN_, int STAGES_, typename OutT, bool PAIR_>
 struct TcCfg {
     static constexpr bool PAIR = PAIR_;
     static constexpr bool WIDE = BN_ == 512;
-    static constexpr int MMA_N = WIDE ? 256 : BN_;       // N of one MMA instruction
     static constexpr int BM = 128;                       // rows per CTA
     static constexpr int BN = BN_;                       // accumulator columns (MMA N)
     static constexpr int BN_LOCAL = PAIR ? BN / 2 : BN;  // B columns staged per CTA
