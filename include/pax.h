@@ -348,7 +348,9 @@ const char*  pax_status_string(pax_status_t s);
  * (synchronises the device).  Returns PAX_ERR_TIMEOUT if a bounded wait in a
  * kernel expired since the last read, else PAX_OK. */
 pax_status_t pax_device_error(void);
-/* Frees the per-stream split-K workspaces this library allocated. */
+/* Frees the device memory this library allocated on its own: the skinny
+ * kernel's per-stream workspaces and the planned tile tables of the wide
+ * tensor-core tile.  Later calls allocate them again as needed. */
 void         pax_shutdown(void);
 /* Library version string. */
 const char*  pax_version(void);

@@ -261,6 +261,20 @@ const int* plan_on_device(const TcItemTable* t, int dev, int units, cudaStream_t
 
 }  // namespace
 
+// Frees the planned tables' device copies (pax_shutdown).
+void tc_free_plans() {
+    std::lock_guard<std::mutex> lk(g_plan_mu);
+    for (auto& kv : g_plan_dev) {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(kv.first.second);
+        cudaFree(kv.second);
+        cudaSetDevice(prev);
+    }
+    g_plan_dev.clear();
+    cudaGetLastError();
+}
+
 // Whole-tile rounds the wide shape takes for this problem on `units` pairs:
 // the planner's makespan when it plans, else the round-robin count.
 double tc_wide_rounds(long long M, long long N, long long K, int units) {

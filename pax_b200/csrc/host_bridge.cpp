@@ -375,7 +375,10 @@ pax_status_t pax_device_error(void) {
     return set_status((a | b) ? PAX_ERR_TIMEOUT : PAX_OK);
 }
 
-void pax_shutdown(void) { free_workspaces(); }
+void pax_shutdown(void) {
+    free_workspaces();
+    tc_free_plans();
+}
 
 size_t pax_sizeof_buffer(void) { return sizeof(pax_buffer_t); }
 size_t pax_sizeof_gemm_desc(void) { return sizeof(pax_gemm_desc_t); }

@@ -79,6 +79,7 @@ bool pdl_enabled();
 // Planned mixed-width tiling for the wide shape (default on; PAX_TC_PLAN=0
 // turns it off).
 bool tc_planning_enabled();
+void tc_free_plans();
 // Shared-memory pipeline depth (TMA ring stages) of each kernel variant.
 int tc_stages(int shape);
 int skinny_stages(long long M, int nt);

@@ -166,6 +166,39 @@ def test_algorithm_selection():
     assert sel(d) == Algo.SIMT
 
 
+def test_host_only_queries_without_a_device():
+    """pax_gemm_pipeline_stages launches nothing; without a device it reports
+    0 rather than failing, and bad descriptors also give 0."""
+    assert lib.pax_gemm_pipeline_stages(ctypes.byref(_desc(4096, 4096, 4096))) == 0
+    assert lib.pax_gemm_pipeline_stages(ctypes.byref(_desc(M=-1))) == 0
+
+
+def test_replicated_and_batched_reject_bad_arguments():
+    d = _desc(512, 512, 512)
+    reps = (ctypes.c_void_p * 8)(*([0x1000] * 8))
+    assert lib.pax_gemm_replicated_ex(ctypes.byref(d), reps, 8, None) == pax_b200.Status.INVALID  # > 7
+    bad = (ctypes.c_void_p * 1)(0x1008)  # not 16-byte aligned
+    assert lib.pax_gemm_replicated_ex(ctypes.byref(d), bad, 1, None) == pax_b200.Status.INVALID
+    assert lib.pax_gemm_replicated_ex(ctypes.byref(d), None, 1, None) == pax_b200.Status.INVALID
+    b = pax_b200._lib.GemmBatchedDesc()
+    b.gemm = _desc(64, 64, 64)
+    b.batch = 2
+    b.stride_c = 64 * 64 - 1  # overlapping C items
+    assert lib.pax_gemm_batched_ex(ctypes.byref(b), None) == pax_b200.Status.INVALID
+    b.stride_c = 64 * 64
+    b.stride_a = -8
+    assert lib.pax_gemm_batched_ex(ctypes.byref(b), None) == pax_b200.Status.INVALID
+    b.stride_a = 0
+    b.batch = 0  # nothing to do
+    assert lib.pax_gemm_batched_ex(ctypes.byref(b), None) == pax_b200.Status.OK
+
+
+def test_ipc_helpers_reject_bad_arguments():
+    h = pax_b200._lib.IpcHandle()
+    assert lib.pax_ipc_export(None, ctypes.byref(h)) == pax_b200.Status.INVALID
+    assert lib.pax_ipc_close(ctypes.c_void_p(0x1234)) == pax_b200.Status.INVALID  # never imported
+
+
 def test_status_strings_and_version():
     for s in pax_b200.Status:
         assert lib.pax_status_string(int(s))
