@@ -348,6 +348,13 @@ const char*  pax_status_string(pax_status_t s);
  * (synchronises the device).  Returns PAX_ERR_TIMEOUT if a bounded wait in a
  * kernel expired since the last read, else PAX_OK. */
 pax_status_t pax_device_error(void);
+/* Self-test of the kernels' bounded waits (new; no counterpart in the
+ * reference): launches one thread that waits on an mbarrier nothing arrives
+ * on.  After the library's 2 s wait limit it records a timeout and ends; the
+ * next pax_device_error() returns PAX_ERR_TIMEOUT and the CUDA context stays
+ * usable.  For tests of the failure path; takes about 2 s of GPU time. */
+pax_status_t pax_selftest_bounded_wait(cudaStream_t stream);
+
 /* Frees the device memory this library allocated on its own: the skinny
  * kernel's per-stream workspaces and the planned tile tables of the wide
  * tensor-core tile.  Later calls allocate them again as needed. */

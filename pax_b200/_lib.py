@@ -137,6 +137,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "pax_last_error": ([], i),
         "pax_status_string": ([i], ctypes.c_char_p),
         "pax_device_error": ([], i),
+        "pax_selftest_bounded_wait": ([P], i),
         "pax_shutdown": ([], None),
         "pax_version": ([], ctypes.c_char_p),
         "pax_sizeof_buffer": ([], sz),

@@ -545,6 +545,26 @@ pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, int
     return launch_skinny_nt<128>(p, grid, 0, korder, ws, counters, stream);
 }
 
+// Self-test of the bounded waits (pax_selftest_bounded_wait): one thread
+// waits on an mbarrier that nothing arrives on.  mbar_wait gives up after
+// kWaitTimeoutNs, records PAX_DEVERR_TIMEOUT in this unit's error word and
+// returns false; the kernel then ends normally and the context stays usable.
+__global__ void selftest_wait_kernel() {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        mbar_init(smem_u32(&bar), 1);
+        fence_mbar_init();
+        (void)mbar_wait(smem_u32(&bar), 0, reinterpret_cast<volatile int*>(&abort_flag));
+    }
+}
+
+pax_status_t launch_selftest_wait(cudaStream_t stream) {
+    selftest_wait_kernel<<<1, 32, 0, stream>>>();
+    return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
+}
+
 int read_clear_device_error_skinny() {
     int v = 0, z = 0;
     if (cudaMemcpyFromSymbol(&v, g_pax_device_error, sizeof(int)) != cudaSuccess) return -1;
@@ -585,6 +605,11 @@ static pax_status_t scratch_address(int dev, void** out) {
 }
 
 }  // namespace pax
+
+extern "C" pax_status_t pax_selftest_bounded_wait(cudaStream_t stream) {
+    const pax_status_t st = pax::launch_selftest_wait(stream);
+    return pax::report_status(st, st == PAX_OK ? "" : "pax_selftest_bounded_wait: launch failed");
+}
 
 extern "C" pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cudaStream_t stream) {
     using namespace pax;
