@@ -265,8 +265,9 @@ def decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev, layers: int = 
     """The decode case the skinny kernel is for: `layers` M=16 GEMMs back to
     back, each with its own weights (together 8 x 134 MB, far above L2, so
     every launch streams its B from HBM).  Consecutive launches overlap
-    through programmatic dependent launch: a launch's prologue and first B
-    prefetches run during the previous launch's tail.  Timed per chain with
+    through programmatic dependent launch: a launch's prologue and its first
+    ring of B (weights, marked PAX_GEMM_B_CONST) load during the previous
+    launch's tail.  Timed per chain with
     CUDA events (L2 flushed before each chain); reported per GEMM."""
     import torch
 
@@ -276,7 +277,9 @@ def decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev, layers: int = 
     g.manual_seed(0xDEC0)
     Bs = [(torch.randn((K, N), generator=g, device=dev) * 0.02).half() for _ in range(layers)]
     Cs = [torch.empty((A.shape[0], N), dtype=torch.float16, device=dev) for _ in range(layers)]
-    kw = dict(epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None)
+    # Decode weights are never written by the previous GEMM: PAX_GEMM_B_CONST
+    # lets each launch start streaming its B before the previous one ends.
+    kw = dict(epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None, b_const=True)
 
     def chain():
         for B, C in zip(Bs, Cs):
@@ -298,7 +301,7 @@ def decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev, layers: int = 
     gbs = alg_bytes / (per * 1e-3) / 1e9
     del Bs, Cs
     return {"launches_per_chain": layers, "us_per_gemm": per * 1e3, "achieved": gbs, "frac": gbs / hbm,
-            "pdl": os.environ.get("PAX_PDL", "1") != "0"}
+            "pdl": os.environ.get("PAX_PDL", "1") != "0", "b_const": True}
 
 
 def run_pax(args):

@@ -97,6 +97,14 @@ typedef enum {
     PAX_ALGO_SIMT   = 4  /* CUDA-core kernel for TMA-unaligned problems      */
 } pax_algo_t;
 
+/* Hint bits ORed into pax_gemm_desc_t.algo (new; no counterpart in the
+ * reference).  PAX_GEMM_B_CONST: B is not written by the kernel launched
+ * just before on the same stream (typically weights).  The skinny kernel
+ * then starts copying B into shared memory before that kernel has
+ * finished; A and every write still wait for it.  Leave it unset when the
+ * previous kernel may write B. */
+#define PAX_GEMM_B_CONST 0x100
+
 /* General GEMM descriptor (new).  Zero leading dimensions mean contiguous. */
 typedef struct {
     const void*    A;        /* fp16 [M][lda]                              */

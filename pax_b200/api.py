@@ -47,6 +47,9 @@ class Algo(IntEnum):
     SIMT = 4
 
 
+PAX_GEMM_B_CONST = 0x100  # hint bit of pax_gemm_desc_t.algo (include/pax.h)
+
+
 class PaxError(RuntimeError):
     def __init__(self, status: int, what: str = ""):
         self.status = Status(status)
@@ -101,7 +104,8 @@ def make_desc(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, epilogue="none"
 
 def gemm(A: torch.Tensor, B: torch.Tensor, *, epilogue="none", bias=None, residual=None, alpha: float = 1.0,
          out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16, algo="auto",
-         stream: torch.cuda.Stream | None = None, replicas: list[int] | None = None) -> torch.Tensor:
+         stream: torch.cuda.Stream | None = None, replicas: list[int] | None = None,
+         b_const: bool = False) -> torch.Tensor:
     """C = epilogue(alpha * A @ B) on the current (or given) CUDA stream.
 
     A [M, K] and B [K, N] are float16 row-major CUDA tensors; C is float16 or
@@ -110,10 +114,15 @@ def gemm(A: torch.Tensor, B: torch.Tensor, *, epilogue="none", bias=None, residu
     replicas: device addresses of further buffers with out's shape and pitch
     (usually other GPUs' memory, see pax_b200.dist.ReplicatedC) that the same
     kernel also writes C to.
+    b_const: B is not written by the kernel launched just before on this
+    stream (weights); the skinny kernel may then start reading B before that
+    kernel ends (PAX_GEMM_B_CONST).
     """
     if out is None:
         out = torch.empty((A.shape[0], B.shape[1]), dtype=out_dtype, device=A.device)
     d = make_desc(A, B, out, epilogue, bias, residual, alpha, algo)
+    if b_const:
+        d.algo |= PAX_GEMM_B_CONST
     s = stream if stream is not None else torch.cuda.current_stream(A.device)
     if replicas:
         arr = (ctypes.c_void_p * len(replicas))(*replicas)

@@ -34,6 +34,7 @@ struct SkinnyParams {
     int grid;       // number of CTAs (<= work)
     int slices;     // lockstep layout: K slices per tile (CTA = tile * slices + slice); 0 = stream-K
     int korder;     // stream-K only: visit the CTA's segments last to first
+    int b_early;    // B may be copied to shared memory before the previous grid ends
     float* ws;      // [grid][2][MP][NT] fp32 partial sums
     int* counters;  // [num_tiles], zero between launches
     __half* c16;    // exactly one of c16 / c32 is set
@@ -193,24 +194,43 @@ __global__ void __launch_bounds__(192, 1)
             bool ok = true;
             long long cur = sk_cursor0(p);
             SkSeg sg;
+            int n_early = 0;  // leading stages whose B was issued before the wait
             {
-                // Before waiting for the previous grid: pull this CTA's first
-                // k-blocks of B into L2.  A prefetch only warms the cache, so
-                // it cannot observe data that grid is still writing; every
-                // load into shared memory happens after the wait.
+                // Before waiting for the previous grid, this CTA's first
+                // k-blocks of B (the first segment's first ring-full):
+                //   b_early (the caller promised B is not written by that
+                //   grid): copied into the ring's stages now.  Each stage's
+                //   barrier expects B's bytes without arriving, so it
+                //   completes only after A, issued after the wait, lands too.
+                //   Otherwise: pulled into L2 only.  A prefetch warms the
+                //   cache and cannot observe data that grid is still
+                //   writing; every shared-memory load then follows the wait.
                 long long c0 = cur;
                 SkSeg s0;
                 if (sk_next_seg(p, c0, s0)) {
                     const int n0 = s0.nk < STAGES ? s0.nk : STAGES;
-                    for (int j = 0; j < n0; ++j)
+                    for (int j = 0; j < n0; ++j) {
+                        const int kb = s0.kb0 + j * s0.kstep;
+                        if (p.b_early) {
+                            const uint32_t fb = full0 + 8u * j;
+                            mbar_expect_tx(fb, Cfg::B_BYTES);
+                            const uint32_t bdst = smem_u32(sB + j * Cfg::B_BYTES);
 #pragma unroll
-                        for (int b = 0; b < NT / 64; ++b)
-                            tma_prefetch_l2(&tmB, s0.tile * NT + b * 64, (s0.kb0 + j * s0.kstep) * 64);
+                            for (int b = 0; b < NT / 64; ++b)
+                                tma_load_2d(bdst + b * 8192u, &tmB, fb, s0.tile * NT + b * 64, kb * 64);
+                        } else {
+#pragma unroll
+                            for (int b = 0; b < NT / 64; ++b)
+                                tma_prefetch_l2(&tmB, s0.tile * NT + b * 64, kb * 64);
+                        }
+                    }
+                    if (p.b_early) n_early = n0;
                 }
             }
             pdl_wait();
+            int i_kb = 0;  // k-blocks issued so far by this CTA
             while (ok && sk_next_seg(p, cur, sg))
-            for (int j = 0; j < sg.nk; ++j) {
+            for (int j = 0; j < sg.nk; ++j, ++i_kb) {
                 const int tile = sg.tile;
                 const int kb = sg.kb0 + j * sg.kstep;
                 if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
@@ -218,12 +238,19 @@ __global__ void __launch_bounds__(192, 1)
                     break;
                 }
                 const uint32_t fb = full0 + 8u * stage;
-                mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
-                const uint32_t bdst = smem_u32(sB + stage * Cfg::B_BYTES);
-                // All NT/64 boxes of this k-block together: NT*2 contiguous
-                // bytes of every k-row of B.
+                if (i_kb < n_early) {
+                    // B of this stage is already on its way (issued above,
+                    // same stage, same k-block): arrive with A's bytes only.
+                    mbar_arrive_expect_tx(fb, Cfg::A_BYTES);
+                } else {
+                    mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+                    const uint32_t bdst = smem_u32(sB + stage * Cfg::B_BYTES);
+                    // All NT/64 boxes of this k-block together: NT*2
+                    // contiguous bytes of every k-row of B.
 #pragma unroll
-                for (int j = 0; j < NT / 64; ++j) tma_load_2d(bdst + j * 8192u, &tmB, fb, tile * NT + j * 64, kb * 64);
+                    for (int b = 0; b < NT / 64; ++b)
+                        tma_load_2d(bdst + b * 8192u, &tmB, fb, tile * NT + b * 64, kb * 64);
+                }
                 tma_load_2d(smem_u32(sA + stage * Cfg::A_BYTES), &tmA, fb, kb * 64, 0);
                 issued |= 1u << stage;
                 last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
@@ -498,6 +525,7 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
     p.grid = grid;
     p.slices = slices;
     p.korder = (slices == 0 && korder) ? 1 : 0;
+    p.b_early = (pr.b_const && pdl_enabled()) ? 1 : 0;
     p.ws = ws;
     p.counters = counters;
     p.c16 = pr.c_f16 ? static_cast<__half*>(pr.C) : nullptr;

@@ -174,8 +174,12 @@ static int epilogue_flags(pax_epilogue_t e, pax_dtype_t res_dt, float alpha) {
     return f;
 }
 
+// The algorithm field without its hint bits.
+static pax_algo_t algo_of(const pax_gemm_desc_t* d) { return static_cast<pax_algo_t>((int)d->algo & 0xFF); }
+
 static pax_status_t normalize(const pax_gemm_desc_t* d, Problem* p) {
     if (!d) return fail(PAX_ERR_INVALID, "pax_gemm_ex: NULL descriptor");
+    p->b_const = ((int)d->algo & PAX_GEMM_B_CONST) != 0;
     if (d->M < 0 || d->N < 0 || d->K < 0)
         return fail(PAX_ERR_INVALID, "pax_gemm_ex: negative shape m=%lld n=%lld k=%lld", (long long)d->M,
                     (long long)d->N, (long long)d->K);
@@ -388,7 +392,7 @@ pax_status_t pax_gemm_ex(const pax_gemm_desc_t* desc, cudaStream_t stream) {
     Problem p;
     pax_status_t st = normalize(desc, &p);
     if (st != PAX_OK) return st;
-    return run(p, desc->algo, stream);
+    return run(p, algo_of(desc), stream);
 }
 
 pax_status_t pax_gemm_replicated_ex(const pax_gemm_desc_t* desc, void* const* replicas, int n_replicas,
@@ -403,7 +407,7 @@ pax_status_t pax_gemm_replicated_ex(const pax_gemm_desc_t* desc, void* const* re
             return fail(PAX_ERR_INVALID, "pax_gemm_replicated_ex: replica %d is NULL or not 16-byte aligned", i);
     p.replicas = replicas;
     p.n_replicas = n_replicas;
-    return run(p, desc->algo, stream);
+    return run(p, algo_of(desc), stream);
 }
 
 // ------------------------------------------------------------- CUDA IPC
@@ -505,7 +509,7 @@ pax_status_t pax_gemm_batched_ex(const pax_gemm_batched_desc_t* desc, cudaStream
         const long long rsz = (p.epi.flags & EPI_RES_F32) ? 4 : 2;
         if ((p.sres * rsz) % 16 != 0) p.epi.flags &= ~EPI_RES_VEC;
     }
-    return run(p, desc->gemm.algo, stream);
+    return run(p, algo_of(&desc->gemm), stream);
 }
 
 pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc) {

@@ -29,6 +29,8 @@ struct Problem {
     // buffers (same shape and pitch; usually peer GPUs' memory).
     void* const* replicas = nullptr;
     int n_replicas = 0;
+    // PAX_GEMM_B_CONST: B is not written by the previous kernel in the stream.
+    bool b_const = false;
 };
 
 // Per-device facts the launchers need (cached).

@@ -642,3 +642,22 @@ def test_planned_wide_tiling_epilogues(cuda, rng, monkeypatch, epi, out):
     res = rng.standard_normal((M, N)).astype(np.float16)
     got = run_gemm(A, B, cuda, epi=epi, bias=bias, residual=res, out_dtype=out)
     check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
+
+
+@pytest.mark.parametrize("M", [16, 48])
+def test_b_const_chain(cuda, rng, M):
+    """PAX_GEMM_B_CONST (weights not written by the previous kernel): a chain
+    of skinny GEMMs where each reads the previous output as A and its own
+    constant B, launched back to back, matches the oracle step by step."""
+    N = 512
+    Bs = [(rng.uniform(-1, 1, (N, N)) / 16).astype(np.float16) for _ in range(6)]
+    tB = [to_dev(b, cuda) for b in Bs]
+    X0 = rng.uniform(-1, 1, (M, N)).astype(np.float16)
+    X = to_dev(X0, cuda)
+    ref = X0
+    torch.cuda.synchronize()
+    for i in range(6):
+        X = pax_b200.gemm(X, tB[i], b_const=True)
+        ref = oracle.gemm(ref, Bs[i], out_dtype=np.float16)
+    torch.cuda.synchronize()
+    check(X.cpu().numpy(), ref, np.float16)
