@@ -304,6 +304,42 @@ def decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev, layers: int = 
             "pdl": os.environ.get("PAX_PDL", "1") != "0", "b_const": True}
 
 
+def decode_batched(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev, items: int = 8, reps: int = 20):
+    """The same decode shape as `items` independent problems (one activation
+    and weight matrix each, as for the experts or heads of one layer) in one
+    pax_gemm_batched_ex launch: the skinny kernel streams all items' weights
+    back to back.  Timed per launch with CUDA events (L2 flushed before
+    each); reported per item."""
+    import torch
+
+    import pax_b200
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(0xBA7C)
+    M = A.shape[0]
+    As = torch.randn((items, M, K), generator=g, device=dev).half()
+    Bs = (torch.randn((items, K, N), generator=g, device=dev) * 0.02).half()
+    biases = bias.unsqueeze(0).repeat(items, 1)
+    Cs = torch.empty((items, M, N), dtype=torch.float16, device=dev)
+    kw = dict(epilogue=cfg["epi"], bias=biases if "bias" in cfg["epi"] else None, out=Cs)
+    for _ in range(3):
+        flush.zero_()
+        pax_b200.gemm_batched(As, Bs, **kw)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    torch.cuda._sleep(int(0.02 * 2.0e9))
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        pax_b200.gemm_batched(As, Bs, **kw)
+        e1.record()
+    torch.cuda.synchronize()
+    per = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev) / items
+    gbs = alg_bytes / (per * 1e-3) / 1e9
+    del As, Bs, Cs
+    return {"items_per_launch": items, "us_per_gemm": per * 1e3, "achieved": gbs, "frac": gbs / hbm}
+
+
 def run_pax(args):
     import numpy as np  # noqa: F401
     import torch
@@ -489,7 +525,8 @@ def run_pax(args):
                         "traffic": traffic_from_profiles(args.config),
                         "peak_kind": f"{peak_kind} (copy bandwidth)", "algorithmic_bytes_per_launch": alg_bytes,
                         "tflops": achieved, "best_launch_ms": kernel_ms,
-                        "stream": decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev)}
+                        "stream": decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev),
+                        "batched": decode_batched(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev)}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, dt, rows, threads, kind, _ = cpu_gemm_sample(cfg, args.cpu_seconds, args.seed)

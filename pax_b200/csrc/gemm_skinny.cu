@@ -35,6 +35,13 @@ struct SkinnyParams {
     int slices;     // lockstep layout: K slices per tile (CTA = tile * slices + slice); 0 = stream-K
     int korder;     // stream-K only: visit the CTA's segments last to first
     int b_early;    // B may be copied to shared memory before the previous grid ends
+    // Batched launch (rr = 1): `batch` items of num_tiles tiles each; CTA c
+    // takes whole tiles c, c + grid, ... of all items (no K split).  Tile t
+    // is tile t % num_tiles of item t / num_tiles; the tensor maps are 3-D
+    // with the item as z (za / zb: A / B have one slice per item, else the
+    // items share slice 0).  sc, sbias, sres: element strides between items.
+    int rr, batch, za, zb;
+    long long sc, sbias, sres;
     float* ws;      // [grid][2][MP][NT] fp32 partial sums
     int* counters;  // [num_tiles], zero between launches
     __half* c16;    // exactly one of c16 / c32 is set
@@ -92,11 +99,21 @@ struct SkSeg {
 //             blockIdx.x / slices takes k-blocks s, s + slices, ..., so all
 //             CTAs advance through the same k-rows of B together.
 __device__ __forceinline__ long long sk_cursor0(const SkinnyParams& p) {
+    if (p.rr) return blockIdx.x;
     if (p.slices > 0) return 0;
     return p.korder ? sk_unit_begin(blockIdx.x + 1, p) : sk_unit_begin(blockIdx.x, p);
 }
 __device__ __forceinline__ bool sk_next_seg(const SkinnyParams& p, long long& cursor, SkSeg& sg) {
     const int KB = p.kblocks;
+    if (p.rr) {
+        if (cursor >= (long long)p.batch * p.num_tiles) return false;
+        sg.tile = (int)cursor;
+        sg.kb0 = 0;
+        sg.kstep = 1;
+        sg.nk = KB;
+        cursor += p.grid;
+        return true;
+    }
     if (p.slices > 0) {
         if (cursor != 0) return false;
         cursor = 1;
@@ -209,6 +226,8 @@ __global__ void __launch_bounds__(192, 1)
                 SkSeg s0;
                 if (sk_next_seg(p, c0, s0)) {
                     const int n0 = s0.nk < STAGES ? s0.nk : STAGES;
+                    const int bz0 = s0.tile / p.num_tiles, tl0 = s0.tile - bz0 * p.num_tiles;
+                    const int zb0 = p.zb ? bz0 : 0;
                     for (int j = 0; j < n0; ++j) {
                         const int kb = s0.kb0 + j * s0.kstep;
                         if (p.b_early) {
@@ -217,11 +236,11 @@ __global__ void __launch_bounds__(192, 1)
                             const uint32_t bdst = smem_u32(sB + j * Cfg::B_BYTES);
 #pragma unroll
                             for (int b = 0; b < NT / 64; ++b)
-                                tma_load_2d(bdst + b * 8192u, &tmB, fb, s0.tile * NT + b * 64, kb * 64);
+                                tma_load_3d(bdst + b * 8192u, &tmB, fb, tl0 * NT + b * 64, kb * 64, zb0);
                         } else {
 #pragma unroll
                             for (int b = 0; b < NT / 64; ++b)
-                                tma_prefetch_l2(&tmB, s0.tile * NT + b * 64, kb * 64);
+                                tma_prefetch_l2(&tmB, tl0 * NT + b * 64, kb * 64, zb0);
                         }
                     }
                     if (p.b_early) n_early = n0;
@@ -231,7 +250,8 @@ __global__ void __launch_bounds__(192, 1)
             int i_kb = 0;  // k-blocks issued so far by this CTA
             while (ok && sk_next_seg(p, cur, sg))
             for (int j = 0; j < sg.nk; ++j, ++i_kb) {
-                const int tile = sg.tile;
+                const int bz = sg.tile / p.num_tiles, tile = sg.tile - bz * p.num_tiles;
+                const int za = p.za ? bz : 0, zb = p.zb ? bz : 0;
                 const int kb = sg.kb0 + j * sg.kstep;
                 if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
                     ok = false;
@@ -249,9 +269,9 @@ __global__ void __launch_bounds__(192, 1)
                     // contiguous bytes of every k-row of B.
 #pragma unroll
                     for (int b = 0; b < NT / 64; ++b)
-                        tma_load_2d(bdst + b * 8192u, &tmB, fb, tile * NT + b * 64, kb * 64);
+                        tma_load_3d(bdst + b * 8192u, &tmB, fb, tile * NT + b * 64, kb * 64, zb);
                 }
-                tma_load_2d(smem_u32(sA + stage * Cfg::A_BYTES), &tmA, fb, kb * 64, 0);
+                tma_load_3d(smem_u32(sA + stage * Cfg::A_BYTES), &tmA, fb, kb * 64, 0, za);
                 issued |= 1u << stage;
                 last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
                 if (++stage == STAGES) {
@@ -323,7 +343,7 @@ __global__ void __launch_bounds__(192, 1)
         long long cur = sk_cursor0(p);
         SkSeg sg;
         while (sk_next_seg(p, cur, sg)) {
-            const int tile = sg.tile;
+            const int tile = sg.tile;  // global tile (item * num_tiles + tile) in batched launches
             // All four epilogue warps take the same branch (they meet at named
             // barriers below), so the wait outcome is AND-reduced across them.
             const bool ok = named_barrier_and<1, 128>(mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag));
@@ -394,26 +414,32 @@ __global__ void __launch_bounds__(192, 1)
             }
             if (do_out) {
                 const int flags = p.epi.flags;
+                // Batch item of this tile (0 unless batched) and its operands.
+                const int bz = tile / p.num_tiles, tl = tile - bz * p.num_tiles;
+                const __half* bias = p.epi.bias ? p.epi.bias + (long long)bz * p.sbias : nullptr;
+                const long long res_off = (long long)bz * p.sres;
+                __half* c16 = p.c16 ? p.c16 + (long long)bz * p.sc : nullptr;
+                float* c32 = p.c32 ? p.c32 + (long long)bz * p.sc : nullptr;
 #pragma unroll
                 for (int sb = 0; sb < NSUB; ++sb) {
-                    const long long n = (long long)tile * NT + sb * 128 + n_local;
+                    const long long n = (long long)tl * NT + sb * 128 + n_local;
                     if (n >= p.N) continue;
-                    const float b = (flags & EPI_BIAS) ? __half2float(p.epi.bias[n]) : 0.f;
+                    const float b = (flags & EPI_BIAS) ? __half2float(bias[n]) : 0.f;
 #pragma unroll
                     for (int m = 0; m < MP; ++m) {
                         if (m < p.M) {
                             float r = 0.f;
                             if (flags & EPI_RES) {
-                                const long long off = (long long)m * p.epi.ld_res + n;
+                                const long long off = res_off + (long long)m * p.epi.ld_res + n;
                                 r = (flags & EPI_RES_F32)
                                         ? static_cast<const float*>(p.epi.residual)[off]
                                         : __half2float(static_cast<const __half*>(p.epi.residual)[off]);
                             }
                             const float o = epi_scalar(v[sb][m], b, r, flags, p.epi.alpha);
-                            if (p.c16)
-                                p.c16[(long long)m * p.ldc + n] = __float2half_rn(o);
+                            if (c16)
+                                c16[(long long)m * p.ldc + n] = __float2half_rn(o);
                             else
-                                p.c32[(long long)m * p.ldc + n] = o;
+                                c32[(long long)m * p.ldc + n] = o;
                         }
                     }
                 }
@@ -448,15 +474,18 @@ static PFN_cuTensorMapEncodeTiled_v12000 sk_encoder() {
     return fn;
 }
 
+// 3-D map of `depth` row-major fp16 matrices `zstride` bytes apart (depth 1
+// for a single problem; the stride then only has to satisfy the encoder).
 static bool sk_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch_bytes,
-                    uint32_t box_inner, uint32_t box_outer) {
+                    uint64_t depth, uint64_t zstride, uint32_t box_inner, uint32_t box_outer) {
     auto enc = sk_encoder();
     if (!enc) return false;
-    cuuint64_t dims[2] = {inner, outer};
-    cuuint64_t strides[1] = {pitch_bytes};
-    cuuint32_t box[2] = {box_inner, box_outer};
-    cuuint32_t estr[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+    if (zstride == 0) zstride = ((outer * pitch_bytes) + 15) & ~uint64_t(15);
+    cuuint64_t dims[3] = {inner, outer, depth};
+    cuuint64_t strides[2] = {pitch_bytes, zstride};
+    cuuint32_t box[3] = {box_inner, box_outer, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -513,8 +542,12 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
                                        int* counters, cudaStream_t stream) {
     using Cfg = SkCfg<MP, NT>;
     CUtensorMap tA, tB;
-    if (!sk_tmap(&tA, pr.A, pr.K, pr.M, pr.lda * 2, 64, MP)) return PAX_ERR_CUDA;
-    if (!sk_tmap(&tB, pr.B, pr.N, pr.K, pr.ldb * 2, 64, 64)) return PAX_ERR_CUDA;
+    const bool batched = pr.batch > 1;
+    const bool za = batched && pr.sa > 0, zb = batched && pr.sb > 0;
+    if (!sk_tmap(&tA, pr.A, pr.K, pr.M, pr.lda * 2, za ? pr.batch : 1, za ? pr.sa * 2 : 0, 64, MP))
+        return PAX_ERR_CUDA;
+    if (!sk_tmap(&tB, pr.B, pr.N, pr.K, pr.ldb * 2, zb ? pr.batch : 1, zb ? pr.sb * 2 : 0, 64, 64))
+        return PAX_ERR_CUDA;
     SkinnyParams p;
     p.M = (int)pr.M;
     p.N = (int)pr.N;
@@ -532,7 +565,21 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
     p.c32 = pr.c_f16 ? nullptr : static_cast<float*>(pr.C);
     p.ldc = pr.ldc;
     p.epi = pr.epi;
-    if (grid < 1 || grid > p.work) return PAX_ERR_INVALID;
+    p.rr = batched ? 1 : 0;
+    p.batch = batched ? (int)pr.batch : 1;
+    p.za = za ? 1 : 0;
+    p.zb = zb ? 1 : 0;
+    p.sc = batched ? pr.sc : 0;
+    p.sbias = batched ? pr.sbias : 0;
+    p.sres = batched ? pr.sres : 0;
+    if (batched) {
+        // Whole tiles round-robin over the CTAs: no workspace, no K split.
+        if (slices != 0 || grid < 1 || (long long)grid > (long long)p.batch * p.num_tiles ||
+            (long long)p.batch * p.num_tiles > 0x7fffffffLL)
+            return PAX_ERR_INVALID;
+    } else if (grid < 1 || grid > p.work) {
+        return PAX_ERR_INVALID;
+    }
     if (slices > 0 && slices * p.num_tiles != grid) return PAX_ERR_INVALID;
     auto kern = gemm_skinny_kernel<MP, NT>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES) != cudaSuccess)

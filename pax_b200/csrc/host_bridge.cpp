@@ -260,12 +260,22 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
         }
     }
     pax_status_t st;
-    // The tcgen05 kernel takes a whole batch in one launch (3-D tensor
-    // maps); the skinny and CUDA-core kernels run one launch per item.
     if (p.n_replicas > 0 && algo != PAX_ALGO_TC && algo != PAX_ALGO_TC2)
         return fail(PAX_ERR_UNSUPPORTED, "replicated output needs the tensor-core path (m > %lld, 16-byte aligned rows)",
                     kSkinnyMaxM);
-    if (p.batch > 1 && (algo == PAX_ALGO_SKINNY || algo == PAX_ALGO_SIMT)) {
+    // The tensor-core kernels take a whole batch in one launch (3-D tensor
+    // maps); the skinny kernel as whole (item, tile) units round-robin over
+    // the SMs.  The CUDA-core kernel runs one launch per item.
+    if (p.batch > 1 && algo == PAX_ALGO_SKINNY) {
+        if (!tma_compatible(p) || p.M > kSkinnyMaxM)
+            return fail(PAX_ERR_UNSUPPORTED, "skinny path needs m <= %lld and 16-byte aligned rows", kSkinnyMaxM);
+        const long long units = p.batch * ((p.N + 127) / 128);
+        const int grid = (int)(units < di.sms ? units : di.sms);
+        st = launch_skinny_ws(p, 128, grid, nullptr, nullptr, s, 0, false);
+        if (st != PAX_OK) return fail(st, "launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return set_status(PAX_OK);
+    }
+    if (p.batch > 1 && algo == PAX_ALGO_SIMT) {
         for (long long b = 0; b < p.batch; ++b) {
             st = run(batch_item(p, b), algo, s);
             if (st != PAX_OK) return st;

@@ -176,6 +176,13 @@ __device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int32_t 
                  : "memory");
 }
 
+__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int32_t x, int32_t y, int32_t z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
 // Programmatic dependent launch.  pdl_wait: block until the grid this one
 // depends on (the previous kernel in the stream, when launched with
 // programmatic stream serialization) has completed and its memory is

@@ -661,3 +661,28 @@ def test_b_const_chain(cuda, rng, M):
         ref = oracle.gemm(ref, Bs[i], out_dtype=np.float16)
     torch.cuda.synchronize()
     check(X.cpu().numpy(), ref, np.float16)
+
+
+@pytest.mark.parametrize("shared", ["none", "A", "B"])
+@pytest.mark.parametrize("M", [1, 16, 64])
+def test_batched_skinny_single_launch(cuda, rng, shared, M):
+    """Batched m <= 64 problems in one skinny-kernel launch (whole (item,
+    tile) units round-robin over the SMs): per-item bias and residual, and
+    A or B shared by every item (stride 0)."""
+    nb, N, K = 5, 640, 256
+    A = rng.standard_normal((M, K) if shared == "A" else (nb, M, K)).astype(np.float16)
+    B = (rng.standard_normal((K, N) if shared == "B" else (nb, K, N)) * 0.05).astype(np.float16)
+    bias = rng.standard_normal((nb, N)).astype(np.float16)
+    res = rng.standard_normal((nb, M, N)).astype(np.float16)
+    C = pax_b200.gemm_batched(to_dev(A, cuda), to_dev(B, cuda), epilogue="residual_gelu_tanh",
+                              residual=to_dev(res, cuda))
+    got = C.cpu().numpy()
+    C2 = pax_b200.gemm_batched(to_dev(A, cuda), to_dev(B, cuda), epilogue="bias", bias=to_dev(bias, cuda),
+                               out_dtype=torch.float32)
+    got2 = C2.cpu().numpy()
+    for b in range(nb):
+        a = A if shared == "A" else A[b]
+        bb = B if shared == "B" else B[b]
+        check(got[b], oracle.gemm(a, bb, epi="residual_gelu_tanh", residual=res[b], out_dtype=np.float16),
+              np.float16)
+        check(got2[b], oracle.gemm(a, bb, epi="bias", bias=bias[b], out_dtype=np.float32), np.float32)
