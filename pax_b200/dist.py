@@ -8,7 +8,8 @@ all-gather into the GEMM: each rank's kernel also stores its tiles straight
 into the peers' C over NVLink.  `gather_columns` is the unfused baseline:
 one NCCL all-gather of the contiguous slabs into a [P][M][Ns] staging buffer,
 packed into row-major M x N.  The reference has no multi-GPU code; this is
-the partitioning BASELINE's configuration 5 asks for.
+the partitioning its large benchmark configuration (32768^3 over 1 to 8
+GPUs, B and C split along N) calls for.
 """
 from __future__ import annotations
 

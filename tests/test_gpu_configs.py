@@ -1,4 +1,4 @@
-"""The five BASELINE configurations at full size.
+"""The five benchmark configurations (C1-C5) at full size.
 
 Each run uses seeded device-side inputs with the configuration's shapes and
 distributions.  Two checks:
