@@ -204,15 +204,18 @@ pax_status_t pax_gemm_ex(const pax_gemm_desc_t* desc, cudaStream_t stream);
  * whose GPU memory is owned by their own allocator (a framework's caching
  * allocator, a serving process that reserves memory at start-up) and loops
  * that cannot afford the device synchronisation of cudaMalloc/cudaFree.
- * Same arithmetic as pax_gemm_ex with PAX_ALGO_SKINNY (desc->algo is
- * ignored), but the split-K scratch is a fixed 8 MiB array inside the
- * library, held by every GPU that loads it until the process exits.  Calls
- * no cudaMalloc/cudaFree.  Problems whose scratch need exceeds 8 MiB
- * (roughly m > 48 at 148 SMs) return PAX_ERR_UNSUPPORTED with a message.
- * The first call on a device looks up the array's device address, so make
- * it before any stream capture.  All calls share the array: calls that
- * overlap on the GPU (different streams, or devices sharing nothing but the
- * process) on the same device race and give wrong results. */
+ * Same kernel and epilogue as pax_gemm_ex with PAX_ALGO_SKINNY (desc->algo
+ * is ignored), always in its stream-K layout, so results agree with that
+ * entry point up to fp32 summation order.  The split-K scratch is a fixed
+ * 8 MiB array inside the library, held by every GPU that loads it until the
+ * process exits.  Calls no cudaMalloc/cudaFree.  Problems whose scratch
+ * need exceeds 8 MiB (roughly m > 48 at 148 SMs) return PAX_ERR_UNSUPPORTED
+ * with a message, before anything is launched.  The first call on a device
+ * looks up the array's device address, so make it before any stream
+ * capture.  Each call clears the counters it uses on `stream` first.  Each
+ * device has its own copy of the array, but all calls on one device share
+ * it: calls that overlap on the GPU there (different streams without
+ * ordering between them) race and give wrong results. */
 pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cudaStream_t stream);
 
 /* Batched GEMM (new; generalises the reference's Futhark entry
