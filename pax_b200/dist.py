@@ -13,6 +13,7 @@ GPUs, B and C split along N) calls for.
 """
 from __future__ import annotations
 
+import time
 from typing import Callable
 
 import torch
@@ -81,15 +82,21 @@ class ReplicatedC:
     finished reading the previous contents) and one after it (every rank's
     slab has landed everywhere) bracket each call, on the current stream.
 
+    With a `monitor` (a PeerMonitor), each call first checks on the host
+    that every peer is alive and at the same step, and raises RankFailure
+    before the first all-reduce if one has left or stopped responding.
+
     `_export`, `_import`, `_close` and `gemm_fn` exist so that the host logic
     can be tested without GPUs.
     """
 
     def __init__(self, M: int, N_total: int, dtype: torch.dtype = torch.float16, device=None, group=None, *,
-                 _export: Callable | None = None, _import: Callable | None = None, _close: Callable | None = None):
+                 monitor: PeerMonitor | None = None, _export: Callable | None = None,
+                 _import: Callable | None = None, _close: Callable | None = None):
         from . import api
 
         self.group = group
+        self.monitor = monitor
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if not equal_slabs(N_total, self.world):
@@ -124,6 +131,8 @@ class ReplicatedC:
         if gemm_fn is None:
             from .api import gemm as gemm_fn
         s, e = self.slab
+        if self.monitor is not None:
+            self.monitor.step()
         dist.all_reduce(self._flag, group=self.group)
         gemm_fn(A, B_slab, epilogue=epilogue, bias=bias_slab, residual=residual_slab, out=self.full[:, s:e],
                 replicas=self.replica_addresses())
@@ -134,3 +143,89 @@ class ReplicatedC:
         for ptr in self.peers.values():
             self._close(ptr)
         self.peers = {}
+
+
+class RankFailure(RuntimeError):
+    """A peer rank left the job or stopped making progress.
+
+    Raised on the host by `PeerMonitor.step` before this rank's next launch,
+    so none of this rank's kernels or collectives is left waiting on the
+    missing peer."""
+
+    def __init__(self, rank: int, reason: str):
+        super().__init__(f"rank {rank} {reason}")
+        self.rank = rank
+        self.reason = reason
+
+
+class PeerMonitor:
+    """Host-side failure detection between steps, through the c10d store.
+
+    Ranks of a slab-partitioned job run the same steps in the same order,
+    and a step with a collective (the all-gather of C, or the ordering
+    all-reduces of `ReplicatedC`) cannot finish while a peer is missing.
+    Before each step's launches every rank calls `step()`:
+
+    * it publishes its own step number under ``<name>/step/<rank>``;
+    * it waits until every peer has published the same step number, i.e.
+      every peer is alive and about to launch the same step;
+    * a peer that called `leave()` (a rank leaving between steps) raises
+      `RankFailure(peer, "left ...")` at once;
+    * a peer that has not arrived after `timeout` seconds (a rank that
+      crashed, hangs on the host or never started) raises
+      `RankFailure(peer, "stopped responding ...")`.
+
+    The check costs one store round trip per peer per step (tens of
+    microseconds each on one node), so it suits steps of a millisecond or
+    more.  It does not replace the process group's own timeout, which still
+    bounds a collective whose peer dies inside the step.
+    """
+
+    def __init__(self, timeout: float = 30.0, name: str = "pax_monitor", store=None, group=None,
+                 poll: float = 0.001):
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.timeout = float(timeout)
+        self.poll = float(poll)
+        self.name = name
+        self._store = store if store is not None else dist.distributed_c10d._get_default_store()
+        self._step = 0
+
+    def _key(self, kind: str, rank: int) -> str:
+        return f"{self.name}/{kind}/{rank}"
+
+    def step(self) -> int:
+        """Announce this rank's next step and wait for every peer to reach it.
+        Returns the step number (0 for the first call)."""
+        s = self._step
+        self._store.set(self._key("step", self.rank), str(s))
+        pending = [p for p in range(self.world) if p != self.rank]
+        last = {p: -1 for p in pending}
+        deadline = time.monotonic() + self.timeout
+        wait = self.poll
+        while pending:
+            still = []
+            for p in pending:
+                if self._store.check([self._key("left", p)]):
+                    why = self._store.get(self._key("left", p)).decode()
+                    raise RankFailure(p, f"left the job ({why}) before step {s}")
+                if self._store.check([self._key("step", p)]):
+                    last[p] = int(self._store.get(self._key("step", p)))
+                if last[p] < s:
+                    still.append(p)
+            pending = still
+            if not pending:
+                break
+            if time.monotonic() > deadline:
+                p = pending[0]
+                raise RankFailure(p, f"stopped responding: last step {last[p]}, waited {self.timeout:.1f} s "
+                                     f"at step {s}")
+            time.sleep(wait)
+            wait = min(wait * 2, 0.05)
+        self._step = s + 1
+        return s
+
+    def leave(self, reason: str = "shutdown") -> None:
+        """Tell the peers, between steps, that this rank will launch nothing
+        more.  Their next `step()` raises RankFailure instead of waiting."""
+        self._store.set(self._key("left", self.rank), reason)
