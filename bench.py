@@ -239,6 +239,98 @@ class ClockSampler:
                 "samples": len(sm), "power_w_max": max(pw)}
 
 
+class NvmlSampler:
+    """SM clock, power and clock-event reasons of one GPU through NVML (the
+    library nvidia-smi reads), polled every `interval` seconds on a thread.
+    Each sample carries its host time, so `stop(window)` can keep only the
+    samples taken while the timed steps ran on the GPU.  A timed region of a
+    few milliseconds is invisible to a 50 ms nvidia-smi loop; at 2 ms it
+    gets several samples."""
+
+    REASONS = {  # reported name -> NVML bit (clocks_event_reasons.*)
+        "hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+        "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+        "hw_power_brake_slowdown": "nvmlClocksEventReasonHwPowerBrakeSlowdown",
+        "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+        "sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+        "applications_clocks_setting": "nvmlClocksEventReasonApplicationsClocksSetting",
+        "gpu_idle": "nvmlClocksEventReasonGpuIdle",
+    }
+
+    def __init__(self, pci_bus_id: str | None = None, index: int = 0, interval: float = 0.002, nvml=None):
+        if nvml is None:
+            import pynvml as nvml
+        self.nv = nvml
+        self.nv.nvmlInit()
+        self.h = (self.nv.nvmlDeviceGetHandleByPciBusId(pci_bus_id) if pci_bus_id
+                  else self.nv.nvmlDeviceGetHandleByIndex(index))
+        self.max_mhz = float(self.nv.nvmlDeviceGetMaxClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+        self.bits = {name: getattr(self.nv, attr) for name, attr in self.REASONS.items() if hasattr(self.nv, attr)}
+        self.interval = interval
+        self.samples: list[tuple[float, float, float, int]] = []  # (host time, SM MHz, W, reason mask)
+        self._stop = threading.Event()
+        self._t = None
+
+    def _poll(self):
+        nv, h = self.nv, self.h
+        while not self._stop.is_set():
+            t = time.perf_counter()
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                mask = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+            except Exception:  # a failed query loses one sample, not the run
+                time.sleep(self.interval)
+                continue
+            self.samples.append((t, sm, pw, mask))
+            time.sleep(self.interval)
+
+    def start(self):
+        self._t = threading.Thread(target=self._poll, daemon=True)
+        self._t.start()
+
+    def stop(self, window: tuple[float, float] | None = None):
+        """Summary of the samples whose host time lies in `window` (all of
+        them when None).  If none does, the sample nearest the window's
+        middle stands in, and `samples_in_window` says 0."""
+        self._stop.set()
+        if self._t is not None:
+            self._t.join(timeout=5)
+        try:
+            self.nv.nvmlShutdown()
+        except Exception:
+            pass
+        if not self.samples:
+            return None
+        sel = self.samples
+        if window is not None:
+            sel = [s for s in self.samples if window[0] <= s[0] <= window[1]]
+            if not sel:
+                mid = 0.5 * (window[0] + window[1])
+                sel = [min(self.samples, key=lambda s: abs(s[0] - mid))]
+        mask = 0
+        for s in sel:
+            mask |= s[3]
+        in_window = len([s for s in self.samples if window is None or window[0] <= s[0] <= window[1]])
+        return {"sm_mhz": statistics.median(s[1] for s in sel), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(n for n, b in self.bits.items() if mask & b and n != "gpu_idle"),
+                "samples": len(sel), "samples_in_window": in_window, "power_w_max": max(s[2] for s in sel),
+                "source": f"NVML every {self.interval * 1e3:.0f} ms, samples inside the timed region"}
+
+
+def clock_sampler(dev_index: int):
+    """NVML sampler for the CUDA device `dev_index` (matched by PCI bus id),
+    else the nvidia-smi loop."""
+    try:
+        import torch
+
+        p = torch.cuda.get_device_properties(dev_index)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        return NvmlSampler(pci_bus_id=bus)
+    except Exception:
+        return ClockSampler(dev_index)
+
+
 # ------------------------------------------------------------------ GPU leg
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -427,19 +519,28 @@ def run_pax(args):
     host_step = (time.perf_counter() - t0) / 3
     torch.cuda.synchronize()
     gate_s = min(2.0, 2.0 * host_step * args.steps + 0.01)
-    clocks = ClockSampler(local)
+    clocks = clock_sampler(local)
     clocks.start()
     time.sleep(0.3)
+    # The device is idle here, so `anchor` completes as soon as it is
+    # recorded: its host time maps event times to host times, which picks
+    # out the clock samples taken while the timed steps ran.
+    anchor = torch.cuda.Event(enable_timing=True)
+    anchor.record()
+    t_anchor = time.perf_counter()
+    torch.cuda.nvtx.range_push("timed steps")
     torch.cuda._sleep(int(gate_s * 2.0e9))  # ~cycles at up to 2 GHz
     for i in range(args.steps):
         flush.zero_()
         starts[i].record()
         step()
         stops[i].record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clk = clocks.stop()
+    window = (t_anchor + anchor.elapsed_time(starts[0]) * 1e-3, t_anchor + anchor.elapsed_time(stops[-1]) * 1e-3)
+    clk = clocks.stop(window) if isinstance(clocks, NvmlSampler) else clocks.stop()
     ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
     ms_mean = statistics.mean(ms)
     t = torch.tensor([ms_mean], dtype=torch.float64, device=dev)
