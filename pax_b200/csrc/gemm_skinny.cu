@@ -34,6 +34,11 @@ struct SkinnyParams {
     int grid;       // number of CTAs (<= work)
     int slices;     // lockstep layout: K slices per tile (CTA = tile * slices + slice); 0 = stream-K
     int korder;     // stream-K only: visit the CTA's segments last to first
+    // Lockstep layout with one slice per tile only: CTAs in groups of
+    // rot_group start their k loop at different k-blocks (group g at
+    // g * kblocks / groups, wrapping around), so that fewer CTAs read the same
+    // k-block of A at the same time.  0 = every CTA starts at k-block 0.
+    int rot_group;
     int b_early;    // B may be copied to shared memory before the previous grid ends
     // Batched launch (rr = 1): `batch` items of num_tiles tiles each; CTA c
     // takes whole tiles c, c + grid, ... of all items (no K split).  Tile t
@@ -146,6 +151,34 @@ __device__ __forceinline__ bool sk_next_seg(const SkinnyParams& p, long long& cu
     return true;
 }
 
+// One output value of the generic epilogue (scale, bias, residual R[off],
+// GeLU), kept out of line: see the output loop of gemm_skinny_kernel.
+__device__ __noinline__ float sk_epi_value(float acc, float b, int flags, float alpha, const void* residual,
+                                           long long off) {
+    float r = 0.f;
+    if (flags & EPI_RES)
+        r = (flags & EPI_RES_F32) ? static_cast<const float*>(residual)[off]
+                                  : __half2float(static_cast<const __half*>(residual)[off]);
+    return epi_scalar(acc, b, r, flags, alpha);
+}
+
+// First k-block of this CTA's rotated k loop (0 without rotation); always
+// in [0, kblocks).
+__device__ __forceinline__ int sk_rotation(const SkinnyParams& p) {
+    if (p.rot_group <= 0) return 0;
+    const int groups = (p.grid + p.rot_group - 1) / p.rot_group;
+    return (int)(((long long)((int)blockIdx.x / p.rot_group) * p.kblocks) / groups);
+}
+// k-block of step j of segment sg.  With a rotation (one segment covering
+// every k-block, kb0 = 0, kstep = 1) the sequence wraps: every k-block is
+// still visited exactly once.
+__device__ __forceinline__ int sk_kblock(const SkinnyParams& p, const SkSeg& sg, int j, int rot) {
+    int kb = sg.kb0 + j * sg.kstep;
+    kb += rot;
+    if (kb >= p.kblocks) kb -= p.kblocks;
+    return kb;
+}
+
 template <int MP, int NT>
 __global__ void __launch_bounds__(192, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -173,6 +206,7 @@ __global__ void __launch_bounds__(192, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int KB = p.kblocks;
+    const int rot = sk_rotation(p);  // first k-block of this CTA's k loop
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -229,7 +263,7 @@ __global__ void __launch_bounds__(192, 1)
                     const int bz0 = s0.tile / p.num_tiles, tl0 = s0.tile - bz0 * p.num_tiles;
                     const int zb0 = p.zb ? bz0 : 0;
                     for (int j = 0; j < n0; ++j) {
-                        const int kb = s0.kb0 + j * s0.kstep;
+                        const int kb = sk_kblock(p, s0, j, rot);
                         if (p.b_early) {
                             const uint32_t fb = full0 + 8u * j;
                             mbar_expect_tx(fb, Cfg::B_BYTES);
@@ -252,7 +286,7 @@ __global__ void __launch_bounds__(192, 1)
             for (int j = 0; j < sg.nk; ++j, ++i_kb) {
                 const int bz = sg.tile / p.num_tiles, tile = sg.tile - bz * p.num_tiles;
                 const int za = p.za ? bz : 0, zb = p.zb ? bz : 0;
-                const int kb = sg.kb0 + j * sg.kstep;
+                const int kb = sk_kblock(p, sg, j, rot);
                 if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
                     ok = false;
                     break;
@@ -420,26 +454,33 @@ __global__ void __launch_bounds__(192, 1)
                 const long long res_off = (long long)bz * p.sres;
                 __half* c16 = p.c16 ? p.c16 + (long long)bz * p.sc : nullptr;
                 float* c32 = p.c32 ? p.c32 + (long long)bz * p.sc : nullptr;
+                // This code runs once per tile, from a cold instruction cache,
+                // unrolled over the MP rows.  fp16 output with at most a bias
+                // (the decode case) is straight-line code; every other
+                // epilogue calls one out-of-line copy per value, so that the
+                // unrolled rows do not each carry the residual and GeLU code.
+                const bool has_bias = (flags & EPI_BIAS) != 0;
+                const bool lean = c16 != nullptr && (flags & (EPI_RES | EPI_GELU_TANH | EPI_GELU_ERF | EPI_SCALE)) == 0;
 #pragma unroll
                 for (int sb = 0; sb < NSUB; ++sb) {
                     const long long n = (long long)tl * NT + sb * 128 + n_local;
                     if (n >= p.N) continue;
-                    const float b = (flags & EPI_BIAS) ? __half2float(bias[n]) : 0.f;
+                    const float b = has_bias ? __half2float(bias[n]) : 0.f;
+                    if (lean) {
 #pragma unroll
-                    for (int m = 0; m < MP; ++m) {
-                        if (m < p.M) {
-                            float r = 0.f;
-                            if (flags & EPI_RES) {
-                                const long long off = res_off + (long long)m * p.epi.ld_res + n;
-                                r = (flags & EPI_RES_F32)
-                                        ? static_cast<const float*>(p.epi.residual)[off]
-                                        : __half2float(static_cast<const __half*>(p.epi.residual)[off]);
+                        for (int m = 0; m < MP; ++m)
+                            if (m < p.M) c16[(long long)m * p.ldc + n] = __float2half_rn(has_bias ? v[sb][m] + b : v[sb][m]);
+                    } else {
+#pragma unroll
+                        for (int m = 0; m < MP; ++m) {
+                            if (m < p.M) {
+                                const float o = sk_epi_value(v[sb][m], b, flags, p.epi.alpha, p.epi.residual,
+                                                             res_off + (long long)m * p.epi.ld_res + n);
+                                if (c16)
+                                    c16[(long long)m * p.ldc + n] = __float2half_rn(o);
+                                else
+                                    c32[(long long)m * p.ldc + n] = o;
                             }
-                            const float o = epi_scalar(v[sb][m], b, r, flags, p.epi.alpha);
-                            if (c16)
-                                c16[(long long)m * p.ldc + n] = __float2half_rn(o);
-                            else
-                                c32[(long long)m * p.ldc + n] = o;
                         }
                     }
                 }
@@ -537,6 +578,8 @@ void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int
     *counter_bytes = (size_t)tiles * sizeof(int);
 }
 
+int skinny_rotation_group();
+
 template <int MP, int NT>
 static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, bool korder, float* ws,
                                        int* counters, cudaStream_t stream) {
@@ -558,6 +601,9 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
     p.grid = grid;
     p.slices = slices;
     p.korder = (slices == 0 && korder) ? 1 : 0;
+    // A rotation keeps each slice's k-blocks a whole lap only with one slice
+    // per tile, outside batched launches.
+    p.rot_group = (slices == 1 && !batched) ? skinny_rotation_group() : 0;
     p.b_early = (pr.b_const && pdl_enabled()) ? 1 : 0;
     p.ws = ws;
     p.counters = counters;
@@ -607,6 +653,17 @@ static pax_status_t launch_skinny_nt(const Problem& p, int grid, int slices, boo
         case 48: return launch_skinny_impl<48, NT>(p, grid, slices, korder, ws, counters, stream);
         default: return launch_skinny_impl<64, NT>(p, grid, slices, korder, ws, counters, stream);
     }
+}
+
+// PAX_SKINNY_ROT=g: in the lockstep layout, CTAs in groups of g start their
+// k loop at different k-blocks (0, the default, starts every CTA at 0).
+int skinny_rotation_group() {
+    static const int g = [] {
+        const char* v = getenv("PAX_SKINNY_ROT");
+        const int x = v ? atoi(v) : 0;
+        return x > 0 ? x : 0;
+    }();
+    return g;
 }
 
 // nt: 128 or 256 output columns per unit.  slices > 0: lockstep layout (nt
