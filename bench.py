@@ -64,7 +64,23 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--epilogue", default=None, help="override the configuration's epilogue (diagnostics)")
+    ap.add_argument("--m", type=int, default=None, help="override the configuration's M (diagnostics)")
     return ap.parse_args()
+
+
+def config_for(args) -> dict:
+    """The selected configuration with the diagnostic overrides applied; a
+    line measured with an override names it in its workload."""
+    cfg = dict(CONFIGS[args.config])
+    if args.epilogue:
+        cfg["epi"] = args.epilogue
+        cfg["name"] += f" [epilogue overridden: {args.epilogue}]"
+    if args.m is not None:
+        if args.m < 1:
+            raise SystemExit("--m must be positive")
+        cfg["M"] = args.m
+        cfg["name"] += f" [M overridden: {args.m}]"
+    return cfg
 
 
 def rank_env():
@@ -127,7 +143,7 @@ def run_reference(args):
     rank, world, _ = rank_env()
     if rank != 0:
         return 0
-    cfg = CONFIGS[args.config]
+    cfg = config_for(args)
     per_step = max(2.0, min(args.cpu_seconds, 150.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
         cpu_gemm_sample(cfg, per_step, args.seed)
@@ -446,10 +462,7 @@ def run_pax(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    cfg = dict(CONFIGS[args.config])
-    if args.epilogue:
-        cfg["epi"] = args.epilogue
-        cfg["name"] += f" [epilogue overridden: {args.epilogue}]"
+    cfg = config_for(args)
     from pax_b200.dist import ReplicatedC, equal_slabs, gather_columns, slab_bounds
 
     M, K = cfg["M"], cfg["K"]

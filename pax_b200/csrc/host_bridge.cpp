@@ -131,7 +131,12 @@ static pax_status_t get_workspace(int dev, cudaStream_t s, size_t cnt_need, size
             w = Workspace();
             return PAX_ERR_ALLOC;
         }
-        if (cudaMemsetAsync(w.ptr, 0, cnt_cap + ws_cap, s) != cudaSuccess) return PAX_ERR_CUDA;
+        if (cudaMemsetAsync(w.ptr, 0, cnt_cap + ws_cap, s) != cudaSuccess) {
+            // Counters of unknown value must never be used: drop the buffer.
+            cudaFree(w.ptr);
+            w = Workspace();
+            return PAX_ERR_CUDA;
+        }
         w.cnt_cap = cnt_cap;
         w.ws_cap = ws_cap;
     }
