@@ -226,6 +226,34 @@ def test_gemm_ex_rejects_bad_arguments_before_touching_the_device():
     assert lib.pax_gemm_ex(ctypes.byref(d), None) == pax_b200.Status.OK
 
 
+def test_last_error_is_per_thread():
+    """pax_last_error() is thread-local: a thread's failing call does not
+    change the status another thread reads after its own successful call."""
+    import threading
+
+    barrier = threading.Barrier(8)
+    results = {}
+
+    def worker(i):
+        bad = i % 2 == 0
+        d = _desc(M=-1) if bad else _desc(M=0)  # M = 0: valid and empty, returns OK
+        barrier.wait()  # all threads call at the same time
+        for _ in range(200):
+            st = lib.pax_gemm_ex(ctypes.byref(d), None)
+            last = lib.pax_last_error()
+            if st != last or st != (pax_b200.Status.INVALID if bad else pax_b200.Status.OK):
+                results[i] = (st, last)
+                return
+        results[i] = "ok"
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in range(8)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=60)
+    assert results == {i: "ok" for i in range(8)}
+
+
 def test_algorithm_selection():
     sel = lambda d: Algo(lib.pax_gemm_select_algo(ctypes.byref(d)))  # noqa: E731
     assert sel(_desc(4096, 4096, 4096)) == Algo.TC
