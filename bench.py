@@ -65,6 +65,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--epilogue", default=None, help="override the configuration's epilogue (diagnostics)")
     ap.add_argument("--m", type=int, default=None, help="override the configuration's M (diagnostics)")
+    ap.add_argument("--no-subrecords", action="store_true",
+                    help="headline only: skip the other configurations, the collective and the sustained run")
     return ap.parse_args()
 
 
@@ -448,6 +450,256 @@ def decode_batched(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev, items: int = 
     return {"items_per_launch": items, "us_per_gemm": per * 1e3, "achieved": gbs, "frac": gbs / hbm}
 
 
+def make_operands(cfg, M, N, K, dev, seed, rank=0):
+    """Seeded synthetic operands of a configuration on the device: A is the
+    same on every rank; B, bias and residual are this rank's column slab."""
+    import torch
+
+    ga = torch.Generator(device=dev)
+    ga.manual_seed(seed)  # A is replicated: same on every rank
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 1000 * (rank + 1))  # this rank's column slab of B, bias
+    if cfg["dist"] == "uniform":
+        A = (torch.rand((M, K), generator=ga, device=dev) * 2 - 1).half()
+        B = (torch.rand((K, N), generator=g, device=dev) * 2 - 1).half()
+    else:
+        A = torch.randn((M, K), generator=ga, device=dev).half()
+        B = (torch.randn((K, N), generator=g, device=dev) * 0.02).half()
+    bias = torch.randn((N,), generator=g, device=dev).half()
+    res = torch.randn((M, N), generator=g, device=dev).half() if "residual" in cfg["epi"] else None
+    return A, B, bias, res
+
+
+class L2Flush:
+    """Between steps: write a buffer larger than L2, then read a second one,
+    so the dirty lines are written back before the timed launch rather than
+    during it."""
+
+    def __init__(self, dev):
+        import torch
+
+        self.w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def zero_(self):
+        self.w.zero_()
+        self.r.sum()
+
+
+def timed_steps(step, steps, warmup, flush, dev, world, local):
+    """`warmup` untimed steps, then exactly `steps` timed ones, each preceded
+    by an L2 flush and bracketed by CUDA events on the current stream.  The
+    timed loop is queued behind a device-side sleep, so no host launch
+    latency falls between a start and a stop event; a barrier and a
+    synchronize come before and after it.  Returns the per-step times, the
+    max over ranks of their mean, and the clock samples taken inside the
+    timed region."""
+    import torch
+    import torch.distributed as dist
+
+    for _ in range(warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    # Host cost of enqueueing one step, to size the device-side sleep.
+    t0 = time.perf_counter()
+    for _ in range(2):
+        flush.zero_()
+        step()
+    host_step = (time.perf_counter() - t0) / 2
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    gate_s = min(2.0, 2.0 * host_step * steps + 0.01)
+    clocks = clock_sampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    # The device is idle here, so `anchor` completes as soon as it is
+    # recorded: its host time maps event times to host times, which picks
+    # out the clock samples taken while the timed steps ran.
+    anchor = torch.cuda.Event(enable_timing=True)
+    anchor.record()
+    t_anchor = time.perf_counter()
+    torch.cuda.nvtx.range_push("timed steps")
+    torch.cuda._sleep(int(gate_s * 2.0e9))  # ~cycles at up to 2 GHz
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record()
+        step()
+        stops[i].record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    window = (t_anchor + anchor.elapsed_time(starts[0]) * 1e-3, t_anchor + anchor.elapsed_time(stops[-1]) * 1e-3)
+    clk = clocks.stop(window) if isinstance(clocks, NvmlSampler) else clocks.stop()
+    ms = [a.elapsed_time(b) for a, b in zip(starts, stops)]
+    mean = statistics.mean(ms)
+    t = torch.tensor([mean], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if clk is not None:
+        # Cycles per step at the median SM clock of the timed region.
+        clk["kcycles_per_step_at_median"] = mean * clk["sm_mhz"]
+    return {"ms": ms, "mean": mean, "max_over_ranks": float(t.item()), "clocks": clk}
+
+
+def kernel_name(A, B, C, **kw):
+    """Which kernel pax_gemm_ex runs for the problem (host-side queries)."""
+    import pax_b200
+
+    algo = pax_b200.select_algo(A, B, C, **kw).name.lower()
+    d = pax_b200.make_desc(A, B, C, **kw)
+    smem = int(pax_b200.lib.pax_gemm_smem_bytes(ctypes.byref(d)))
+    return {"algo": algo, "stages": pax_b200.pipeline_stages(A, B, C, **kw), "dynamic_smem_bytes": smem}
+
+
+def lean_bound(frac, stages):
+    return {"stages": stages, "bound_frac": (1 - 1 / stages) if stages else None, "measured_frac_of_roof": frac,
+            "holds": (frac >= 1 - 1 / stages) if (frac is not None and stages) else None}
+
+
+def config_record(cfg_id, args, dev, flush, peak, hbm, steps, warmup):
+    """Device-timed sub-record of one configuration at N=1: ms per launch,
+    TFLOP/s, roofline fraction against the measured peaks, the committed
+    ncu DRAM traffic over the algorithmic bytes, the Lean pipeline-bound
+    check and the clocks of its timed region."""
+    import torch
+
+    import pax_b200
+
+    cfg = CONFIGS[cfg_id]
+    M, N, K = cfg["M"], cfg["N"], cfg["K"]
+    A, B, bias, res = make_operands(cfg, M, N, K, dev, args.seed)
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    kw = dict(epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None, residual=res)
+    r = timed_steps(lambda: pax_b200.gemm(A, B, out=C, **kw), steps, warmup, flush, dev, 1, dev.index)
+    flops = 2.0 * M * N * K
+    alg_bytes = 2 * (M * K + K * N + M * N) + (2 * N if "bias" in cfg["epi"] else 0) + (
+        2 * M * N if res is not None else 0)
+    tf = flops / (r["mean"] * 1e-3) / 1e12
+    traffic = traffic_from_profiles(cfg_id)
+    info = kernel_name(A, B, C, **kw)
+    rec = {"workload": cfg["name"], "steps": steps, "warmup": warmup, "ms_per_launch": r["mean"],
+           "best_ms": min(r["ms"]), "tflops": tf, "kernel": info, "clocks": r["clocks"]}
+    if cfg_id == 4:
+        gbs = alg_bytes / (r["mean"] * 1e-3) / 1e9
+        rec["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                           "algorithmic_bytes_per_launch": alg_bytes, "traffic": traffic,
+                           "traffic_over_algorithmic": traffic / alg_bytes if traffic else None}
+        rec["single"] = {"us_per_gemm": r["mean"] * 1e3, "achieved": gbs, "frac": gbs / hbm}
+        rec["noalloc"] = noalloc_record(A, B, bias, C, cfg, alg_bytes, hbm, flush, dev, steps, warmup)
+        rec["stream"] = decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev)
+        rec["batched"] = decode_batched(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev)
+    else:
+        rec["roofline"] = {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                           "algorithmic_bytes_per_launch": alg_bytes, "traffic": traffic,
+                           "traffic_over_algorithmic": traffic / alg_bytes if traffic else None}
+    rec["lean_pipeline_bound"] = lean_bound(rec["roofline"]["frac"], info["stages"])
+    del A, B, bias, res, C
+    torch.cuda.empty_cache()
+    return rec
+
+
+def noalloc_record(A, B, bias, C, cfg, alg_bytes, hbm, flush, dev, steps, warmup):
+    """pax_gemm_skinny_noalloc on the same problem (its per-call counter
+    clear included), timed like the single launch."""
+    import torch
+
+    import pax_b200
+
+    d = pax_b200.make_desc(A, B, C, epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None)
+    lib = pax_b200.lib
+
+    def step():
+        st = lib.pax_gemm_skinny_noalloc(ctypes.byref(d), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+        if st != 0:
+            raise RuntimeError(f"pax_gemm_skinny_noalloc: status {st}")
+
+    r = timed_steps(step, steps, warmup, flush, dev, 1, dev.index)
+    gbs = alg_bytes / (r["mean"] * 1e-3) / 1e9
+    return {"us_per_gemm": r["mean"] * 1e3, "achieved": gbs, "frac": gbs / hbm,
+            "launches_per_call": 2, "note": "a 256-byte counter clear (cudaMemsetAsync) and the GEMM"}
+
+
+def split_record(args, dev, flush, peak, world, rank, local, steps, warmup, gather_too):
+    """C5 (32768^3 BiasGeLU) strong-scaled: the N columns are split over the
+    ranks, so total work is fixed as N grows.  Timed without replication
+    and, at N > 1, with C replicated on every rank by the fused GEMM +
+    all-gather (ReplicatedC)."""
+    import torch
+
+    import pax_b200
+    from pax_b200.dist import ReplicatedC, slab_bounds
+
+    cfg = CONFIGS[5]
+    M, K, n_total = cfg["M"], cfg["K"], cfg["N"]
+    s0, s1 = slab_bounds(n_total, world, rank)
+    A, B, bias, _ = make_operands(cfg, M, s1 - s0, K, dev, args.seed, rank)
+    C = torch.empty((M, s1 - s0), dtype=torch.float16, device=dev)
+    flops = 2.0 * M * n_total * K
+    r = timed_steps(lambda: pax_b200.gemm(A, B, out=C, epilogue=cfg["epi"], bias=bias), steps, warmup, flush, dev,
+                    world, local)
+    rec = {"workload": cfg["name"] + f", N split over {world} GPU(s) (strong scaling)", "steps": steps,
+           "warmup": warmup, "ms_per_step": r["max_over_ranks"], "tflops_total": flops / (r["max_over_ranks"] * 1e-3) / 1e12,
+           "clocks": r["clocks"]}
+    rec["frac_of_peak_per_gpu"] = rec["tflops_total"] / world / peak
+    rec["kernel"] = kernel_name(A, B, C, epilogue=cfg["epi"], bias=bias)
+    del C
+    if gather_too and world > 1:
+        rc = ReplicatedC(M, n_total, device=dev)
+        g = timed_steps(lambda: rc.gemm_slab(A, B, cfg["epi"], bias), steps, warmup, flush, dev, world, local)
+        rec["replicated_fused"] = {"ms_per_step": g["max_over_ranks"],
+                                   "tflops_total": flops / (g["max_over_ranks"] * 1e-3) / 1e12,
+                                   "bytes_pushed_per_rank": M * (s1 - s0) * 2 * (world - 1)}
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        rc.close()
+        del rc
+    del A, B, bias
+    torch.cuda.empty_cache()
+    return rec
+
+
+def gather_record(A, B, bias, res, cfg, M, N, n_total, dev, flush, world, local, steps, warmup):
+    """The C2 step with C replicated on every rank, two ways: the fused GEMM
+    + all-gather (epilogue TMA stores to every peer over NVLink, ordered by
+    two one-element all-reduces) and the GEMM followed by an NCCL
+    all-gather of the slabs and a pack into row-major C."""
+    import torch
+    import torch.distributed as dist
+
+    import pax_b200
+    from pax_b200.dist import ReplicatedC, gather_columns
+
+    flops = 2.0 * M * n_total * cfg["K"]
+    rc = ReplicatedC(M, n_total, device=dev)
+    kb = bias if "bias" in cfg["epi"] else None
+    f = timed_steps(lambda: rc.gemm_slab(A, B, cfg["epi"], kb, res), steps, warmup, flush, dev, world, local)
+    torch.cuda.synchronize()
+    dist.barrier()
+    rc.close()
+    del rc
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+
+    def nccl_step():
+        pax_b200.gemm(A, B, out=C, epilogue=cfg["epi"], bias=kb, residual=res)
+        gather_columns(C)
+
+    n = timed_steps(nccl_step, steps, warmup, flush, dev, world, local)
+    torch.cuda.empty_cache()
+    slab = M * N * 2
+    return {"fused": {"ms_per_step": f["max_over_ranks"], "tflops_total": flops / (f["max_over_ranks"] * 1e-3) / 1e12,
+                      "how": "epilogue TMA stores to every peer's C over NVLink + 2 one-element NCCL all-reduces"},
+            "nccl": {"ms_per_step": n["max_over_ranks"], "tflops_total": flops / (n["max_over_ranks"] * 1e-3) / 1e12,
+                     "how": "GEMM, then NCCL all_gather_into_tensor of the slabs and a pack into row-major C"},
+            "bytes_per_rank_to_peers": slab * (world - 1)}
+
+
 def run_pax(args):
     import numpy as np  # noqa: F401
     import torch
@@ -475,33 +727,10 @@ def run_pax(args):
         n_total = N * world
     if args.gather and not (equal_slabs(n_total, world) or world == 1):
         raise SystemExit("--gather needs equal slabs (N divisible by 8 * ranks)")
-    ga = torch.Generator(device=dev)
-    ga.manual_seed(args.seed)  # A is replicated: same on every rank
-    g = torch.Generator(device=dev)
-    g.manual_seed(args.seed + 1000 * (rank + 1))  # this rank's column slab of B, bias
-    if cfg["dist"] == "uniform":
-        A = (torch.rand((M, K), generator=ga, device=dev) * 2 - 1).half()
-        B = (torch.rand((K, N), generator=g, device=dev) * 2 - 1).half()
-    else:
-        A = torch.randn((M, K), generator=ga, device=dev).half()
-        B = (torch.randn((K, N), generator=g, device=dev) * 0.02).half()
-    bias = torch.randn((N,), generator=g, device=dev).half()
-    res = torch.randn((M, N), generator=g, device=dev).half() if "residual" in cfg["epi"] else None
+    A, B, bias, res = make_operands(cfg, M, N, K, dev, args.seed, rank)
     C = torch.empty((M, N), dtype=torch.float16, device=dev)
     gathered = args.gather and world > 1
-    # L2 flush between steps: write a buffer larger than L2, then read a second
-    # one so the dirty lines are written back before the timed launch rather
-    # than during it.
-    flush_w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    flush_r = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-
-    class _Flush:
-        @staticmethod
-        def zero_():
-            flush_w.zero_()
-            flush_r.sum()
-
-    flush = _Flush()
+    flush = L2Flush(dev)
     kw = dict(epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None, residual=res, out=C)
 
     rc = ReplicatedC(M, n_total, device=dev) if gathered and args.gather_impl == "fused" else None
@@ -514,52 +743,10 @@ def run_pax(args):
         if gathered:
             gather_columns(C)
 
-    for _ in range(args.warmup):
-        flush.zero_()
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    # Host cost of enqueueing one step, so that the whole timed loop can be
-    # queued behind a device-side sleep: the GPU then runs the steps back to
-    # back and no host launch latency falls between a start and stop event.
-    t0 = time.perf_counter()
-    for _ in range(3):
-        flush.zero_()
-        step()
-    host_step = (time.perf_counter() - t0) / 3
-    torch.cuda.synchronize()
-    gate_s = min(2.0, 2.0 * host_step * args.steps + 0.01)
-    clocks = clock_sampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    # The device is idle here, so `anchor` completes as soon as it is
-    # recorded: its host time maps event times to host times, which picks
-    # out the clock samples taken while the timed steps ran.
-    anchor = torch.cuda.Event(enable_timing=True)
-    anchor.record()
-    t_anchor = time.perf_counter()
-    torch.cuda.nvtx.range_push("timed steps")
-    torch.cuda._sleep(int(gate_s * 2.0e9))  # ~cycles at up to 2 GHz
-    for i in range(args.steps):
-        flush.zero_()
-        starts[i].record()
-        step()
-        stops[i].record()
-    torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    window = (t_anchor + anchor.elapsed_time(starts[0]) * 1e-3, t_anchor + anchor.elapsed_time(stops[-1]) * 1e-3)
-    clk = clocks.stop(window) if isinstance(clocks, NvmlSampler) else clocks.stop()
-    ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
-    ms_mean = statistics.mean(ms)
-    t = torch.tensor([ms_mean], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    main = timed_steps(step, args.steps, args.warmup, flush, dev, world, local)
+    ms = main["ms"]
+    ms_max = main["max_over_ranks"]
+    clk = main["clocks"]
     flops_rank = 2.0 * M * N * K
     flops_total = 2.0 * M * n_total * K
     value = flops_total / (ms_max * 1e-3) / 1e12
@@ -602,23 +789,24 @@ def run_pax(args):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    main = torch.cuda.current_stream(dev)
+    cur = torch.cuda.current_stream(dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(main)
+    e0.record(cur)
     for sl in slots:
-        sl["stream"].wait_stream(main)
+        sl["stream"].wait_stream(cur)
     for i in range(e2e_steps):
         e2e_step(i)
     for sl in slots:
-        main.wait_stream(sl["stream"])
-    e1.record(main)
+        cur.wait_stream(sl["stream"])
+    e1.record(cur)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = flops_total / (float(t.item()) * 1e-3) / 1e12
+    del slots, hA, hB, hbias, hres
 
     peak, hbm, peak_kind = peaks()
     stages = pax_b200.pipeline_stages(A, B, C, epilogue=cfg["epi"], bias=bias if "bias" in cfg["epi"] else None,
@@ -627,13 +815,14 @@ def run_pax(args):
     achieved = None if gathered else flops_rank / (statistics.mean(ms) * 1e-3) / 1e12
     roofline = None
     if achieved is not None:
+        alg_bytes = 2 * (M * K + K * N + M * N) + (2 * N if "bias" in cfg["epi"] else 0) + (
+            2 * M * N if res is not None else 0)
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                     "frac": achieved / peak, "traffic": traffic_from_profiles(args.config),
                     "peak_kind": f"{peak_kind} (bf16 dense burst, MEASURED_PEAKS.json)" if peak_kind == "measured"
                     else "fallback 1.59 PFLOP/s", "algorithmic_flops_per_launch": flops_rank,
-                    "best_launch_ms": kernel_ms}
+                    "algorithmic_bytes_per_launch": alg_bytes, "best_launch_ms": kernel_ms}
         if args.config == 4:
-            alg_bytes = 2 * (M * K + K * N + N + M * N)
             gbs = alg_bytes / (statistics.mean(ms) * 1e-3) / 1e9
             roofline = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                         "traffic": traffic_from_profiles(args.config),
@@ -641,6 +830,39 @@ def run_pax(args):
                         "tflops": achieved, "best_launch_ms": kernel_ms,
                         "stream": decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev),
                         "batched": decode_batched(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev)}
+        if roofline["traffic"]:
+            roofline["traffic_over_algorithmic"] = roofline["traffic"] / alg_bytes
+
+    # ---- sub-records.  At N = 1 the other four configurations, each device-
+    # timed like the headline; at N > 1 the collective: the same step with C
+    # replicated (fused and NCCL), and C5 split over the ranks.
+    sub = {}
+    defaults = args.config == 2 and not args.epilogue and args.m is None and not args.strong and not args.gather
+    if defaults and not args.no_subrecords:
+        if world == 1:
+            sub["configs"] = {}
+            for cid, st, wu in ((1, args.steps, max(3, args.warmup)), (3, min(args.steps, 20), max(3, args.warmup)),
+                                (4, args.steps, max(3, args.warmup))):
+                sub["configs"][f"C{cid}"] = config_record(cid, args, dev, flush, peak, hbm, st, wu)
+        else:
+            sub["gather"] = gather_record(A, B, bias, res, cfg, M, N, n_total, dev, flush, world, local,
+                                          min(args.steps, 20), max(3, args.warmup))
+        # C5 over the ranks: 55 ms per launch on one GPU, so a few steps.
+        c5 = split_record(args, dev, flush, peak, world, rank, local, 3, 3, gather_too=True)
+        if world == 1:
+            a = c5["tflops_total"]
+            c5["roofline"] = {"bound": "tensor", "achieved": a, "peak": peak, "unit": "TFLOP/s", "frac": a / peak,
+                              "traffic": traffic_from_profiles(5)}
+            c5["lean_pipeline_bound"] = lean_bound(a / peak, c5["kernel"]["stages"])
+            sub["configs"]["C5"] = c5
+        else:
+            sub["c5_split"] = c5
+
+    # Clocks over a long back-to-back run of the headline step: enough NVML
+    # samples to say what SM clock the kernel runs at under sustained load.
+    if defaults and world == 1 and not args.no_subrecords:
+        sub["sustained"] = sustained_record(step, dev, local, flops_rank)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, dt, rows, threads, kind, _ = cpu_gemm_sample(cfg, args.cpu_seconds, args.seed)
@@ -671,10 +893,9 @@ def run_pax(args):
                     "pipelining": "steps alternate between 2 streams (each step: upload inputs, GEMM, download C)"},
             "clocks": clk,
             "gpu_launches": args.steps,
-            "lean_pipeline_bound": {"stages": stages, "bound_frac": (1 - 1 / stages) if stages else None,
-                                    "measured_frac_of_roof": roofline["frac"] if roofline else None,
-                                    "holds": (roofline["frac"] >= 1 - 1 / stages) if (roofline and stages) else None},
+            "lean_pipeline_bound": lean_bound(roofline["frac"] if roofline else None, stages),
         }
+        line.update(sub)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -682,6 +903,45 @@ def run_pax(args):
             rc.close()
         dist.destroy_process_group()
     return 0
+
+
+def sustained_record(step, dev, local, flops, seconds=0.25):
+    """The headline step back to back (no L2 flush) for about `seconds`,
+    with NVML clock samples throughout: mean ms per launch, the median SM
+    clock under this load and their product, the cycles one launch takes."""
+    import torch
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    per = max((time.perf_counter() - t0) / 5, 1e-5)
+    n = int(min(20000, max(50, seconds / per)))
+    clocks = clock_sampler(local)
+    clocks.start()
+    time.sleep(0.2)
+    anchor = torch.cuda.Event(enable_timing=True)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    anchor.record()
+    t_anchor = time.perf_counter()
+    torch.cuda._sleep(int(0.05 * 2.0e9))
+    e0.record()
+    for _ in range(n):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    window = (t_anchor + anchor.elapsed_time(e0) * 1e-3, t_anchor + anchor.elapsed_time(e1) * 1e-3)
+    clk = clocks.stop(window) if isinstance(clocks, NvmlSampler) else clocks.stop()
+    ms = e0.elapsed_time(e1) / n
+    rec = {"launches": n, "ms_per_launch": ms, "tflops": flops / (ms * 1e-3) / 1e12, "clocks": clk,
+           "note": "back to back, no L2 flush; same kernel and problem as the headline"}
+    if clk is not None:
+        rec["kcycles_per_launch_at_median_mhz"] = ms * clk["sm_mhz"]
+    return rec
 
 
 def main():

@@ -134,15 +134,20 @@ void pax_gemm_wmma_launch(const __half* A, const __half* B, float* C,
 void pax_gemm_ptx_launch(const __half* A, const __half* B, float* C,
                          int m, int n, int k, cudaStream_t stream);
 
-/* replaces pax_gemm_ptx_smem_bytes, src/rtx_gemm_ptx.cu:308-312; returns the
- * dynamic shared memory of the kernel that pax_gemm_ptx_launch runs. */
+/* replaces pax_gemm_ptx_smem_bytes, src/rtx_gemm_ptx.cu:308-312.  The
+ * reference's launchers always run one kernel; these launchers pick a kernel
+ * per problem, so this returns the dynamic shared memory of the kernel
+ * pax_gemm_ptx_launch runs for the reference's default bench problem
+ * (m = n = k = 4096, fp32 C; src/host_bridge.c:498-500) on the current
+ * device.  pax_gemm_smem_bytes answers for any other problem. */
 size_t pax_gemm_ptx_smem_bytes(void);
 
 /* replaces pax_gemm_pipeline_launch, src/rtx_gemm_pipeline.cu:340-362 (declared src/host_bridge.c:85-87) */
 void pax_gemm_pipeline_launch(const __half* A, const __half* B, float* C,
                               int m, int n, int k, cudaStream_t stream);
 
-/* replaces pax_gemm_pipeline_smem_bytes, src/rtx_gemm_pipeline.cu:331-334 */
+/* replaces pax_gemm_pipeline_smem_bytes, src/rtx_gemm_pipeline.cu:331-334:
+ * as pax_gemm_ptx_smem_bytes, for pax_gemm_pipeline_launch. */
 size_t pax_gemm_pipeline_smem_bytes(void);
 
 /* replaces pax_gemm_bias_gelu_launch, src/rtx_gemm_epilogue.cu:375-392 (declared src/host_bridge.c:91-94).
@@ -171,7 +176,9 @@ void pax_gemm_tma_cluster_launch(const __half* A, const __half* B, float* C,
                                  const void* tmap_A, const void* tmap_B,
                                  const void* tmap_C, cudaStream_t stream);
 
-/* replaces pax_gemm_tma_smem_bytes, src/rtx_gemm_tma.cu:273-275 */
+/* replaces pax_gemm_tma_smem_bytes, src/rtx_gemm_tma.cu:273-275: as
+ * pax_gemm_ptx_smem_bytes, for pax_gemm_tma_cluster_launch (the CTA-pair
+ * kernel). */
 size_t pax_gemm_tma_smem_bytes(void);
 
 /* ---------------------------------------------------------------------------
@@ -204,18 +211,20 @@ pax_status_t pax_gemm_ex(const pax_gemm_desc_t* desc, cudaStream_t stream);
  * whose GPU memory is owned by their own allocator (a framework's caching
  * allocator, a serving process that reserves memory at start-up) and loops
  * that cannot afford the device synchronisation of cudaMalloc/cudaFree.
- * Same kernel and epilogue as pax_gemm_ex with PAX_ALGO_SKINNY (desc->algo
- * is ignored), always in its stream-K layout, so results agree with that
- * entry point up to fp32 summation order.  The split-K scratch is a fixed
- * 8 MiB array inside the library, held by every GPU that loads it until the
- * process exits.  Calls no cudaMalloc/cudaFree.  Problems whose scratch
- * need exceeds 8 MiB (roughly m > 48 at 148 SMs) return PAX_ERR_UNSUPPORTED
- * with a message, before anything is launched.  The first call on a device
- * looks up the array's device address, so make it before any stream
- * capture.  Each call clears the counters it uses on `stream` first.  Each
- * device has its own copy of the array, but all calls on one device share
- * it: calls that overlap on the GPU there (different streams without
- * ordering between them) race and give wrong results. */
+ * Same kernel, epilogue and work layout as pax_gemm_ex with
+ * PAX_ALGO_SKINNY (desc->algo is ignored): the lockstep layout when there
+ * are no more 128-column tiles than SMs, else stream-K.  The split-K scratch
+ * is a fixed 8 MiB array inside the library, held by every GPU that loads
+ * it until the process exits.  Calls no cudaMalloc/cudaFree.  Problems whose
+ * scratch need exceeds 8 MiB (stream-K above roughly m = 48 at 148 SMs)
+ * return PAX_ERR_UNSUPPORTED with a message, before anything is launched.
+ * The first call on a device (and the first after that device's CUDA
+ * context was reset or re-created, or after pax_shutdown) looks up the
+ * array's device address, so make it before any stream capture.  Each call
+ * clears the counters it uses on `stream` first.  Each device has its own
+ * copy of the array, but all calls on one device share it: calls that
+ * overlap on the GPU there (different streams without ordering between
+ * them) race and give wrong results. */
 pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cudaStream_t stream);
 
 /* Batched GEMM (new; generalises the reference's Futhark entry
@@ -269,6 +278,14 @@ pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc);
  * throughput >= (1 - 1/STAGES) * min(compute, memory) for the kernel that
  * actually runs).  Host-only, launches nothing. */
 int pax_gemm_pipeline_stages(const pax_gemm_desc_t* desc);
+
+/* Dynamic shared memory, in bytes, of the kernel pax_gemm_ex would launch
+ * for desc (desc->algo honoured; AUTO chosen as pax_gemm_ex chooses) on the
+ * current device, 148 SMs assumed without one; 0 for the CUDA-core kernel,
+ * whose shared memory is static (new: the per-problem form of the
+ * reference's *_smem_bytes queries, src/rtx_gemm_pipeline.cu:331-334).
+ * Host-only, launches nothing. */
+size_t pax_gemm_smem_bytes(const pax_gemm_desc_t* desc);
 
 /* ---- Lean-extraction symbols (pax-lean4/PAX/Extraction.lean:32-84) ----
  * The names and signatures PAX's Lean layer exports.  Sizes are 64-bit and
@@ -365,10 +382,19 @@ pax_status_t pax_device_error(void);
  * next pax_device_error() returns PAX_ERR_TIMEOUT and the CUDA context stays
  * usable.  For tests of the failure path; takes about 2 s of GPU time. */
 pax_status_t pax_selftest_bounded_wait(cudaStream_t stream);
+/* Test hook (new; no counterpart in the reference): writes into the skinny
+ * kernel's split-K arrival counters of `stream`'s workspace (the current
+ * device's) what a launch that gave up on a timed-out wait leaves behind.
+ * The next skinny GEMM on that stream must still be correct.  Synchronises
+ * `stream`.  PAX_ERR_INVALID if the stream has no workspace yet. */
+pax_status_t pax_selftest_stale_counters(cudaStream_t stream);
 
 /* Frees the device memory this library allocated on its own: the skinny
  * kernel's per-stream workspaces and the planned tile tables of the wide
- * tensor-core tile.  Later calls allocate them again as needed. */
+ * tensor-core tile.  Later calls allocate them again as needed.  Also
+ * forgets the looked-up device address of pax_gemm_skinny_noalloc's array.
+ * A workspace belongs to (device, stream handle) and, for
+ * cudaStreamPerThread, to the calling host thread as well. */
 void         pax_shutdown(void);
 /* Library version string. */
 const char*  pax_version(void);

@@ -104,6 +104,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "pax_ipc_close": ([P], i),
         "pax_gemm_select_algo": ([ctypes.POINTER(GemmDesc)], i),
         "pax_gemm_pipeline_stages": ([ctypes.POINTER(GemmDesc)], i),
+        "pax_gemm_smem_bytes": ([ctypes.POINTER(GemmDesc)], sz),
         "pax_gemm_skinny_noalloc": ([ctypes.POINTER(GemmDesc), P], i),
         # Lean-extraction names (64-bit sizes, pointers as integers)
         "pax_gemm_wmma_verified": ([u64] * 6, None),
@@ -138,6 +139,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "pax_status_string": ([i], ctypes.c_char_p),
         "pax_device_error": ([], i),
         "pax_selftest_bounded_wait": ([P], i),
+        "pax_selftest_stale_counters": ([P], i),
         "pax_shutdown": ([], None),
         "pax_version": ([], ctypes.c_char_p),
         "pax_sizeof_buffer": ([], sz),

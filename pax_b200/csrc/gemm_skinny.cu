@@ -21,8 +21,11 @@
 #include "epilogue.cuh"
 
 #include <cudaTypedefs.h>
+#include <atomic>
 #include <mutex>
 #include <stdio.h>
+#include <stdlib.h>
+#include <vector>
 
 namespace pax {
 
@@ -48,7 +51,12 @@ struct SkinnyParams {
     int rr, batch, za, zb;
     long long sc, sbias, sres;
     float* ws;      // [grid][2][MP][NT] fp32 partial sums
-    int* counters;  // [num_tiles], zero between launches
+    // [num_tiles] arrival counters of split tiles: (launch epoch << 32) |
+    // arrivals, 0 when free.  A counter left by an earlier launch (one that
+    // gave up on a timed-out wait before its last contributor arrived) has an
+    // older epoch and is restarted, so it cannot elect the wrong last arriver.
+    unsigned long long* counters;
+    unsigned int epoch;  // this launch's epoch, never 0
     __half* c16;    // exactly one of c16 / c32 is set
     float* c32;
     long long ldc;
@@ -421,9 +429,23 @@ __global__ void __launch_bounds__(192, 1)
                 __threadfence();
                 asm volatile("bar.sync 1, 128;" ::: "memory");
                 if (et == 0) {
-                    const int prev = atomicAdd(p.counters + tile, 1);
-                    const int is_last = (prev == c_last - c_first) ? 1 : 0;
-                    if (is_last) p.counters[tile] = 0;  // ready for the next launch
+                    unsigned long long* ctr = p.counters + tile;
+                    const unsigned long long first = ((unsigned long long)p.epoch << 32) | 1ull;
+                    unsigned long long seen = atomicCAS(ctr, 0ull, first);
+                    unsigned int arrivals = 1;
+                    while (seen != 0ull) {
+                        // Same launch: one more arrival.  Older epoch: a
+                        // leftover, restart the count.
+                        const unsigned long long want = (unsigned int)(seen >> 32) == p.epoch ? seen + 1ull : first;
+                        const unsigned long long prev = atomicCAS(ctr, seen, want);
+                        if (prev == seen) {
+                            arrivals = (unsigned int)want;
+                            break;
+                        }
+                        seen = prev;
+                    }
+                    const int is_last = (arrivals == (unsigned int)(c_last - c_first + 1)) ? 1 : 0;
+                    if (is_last) atomicExch(ctr, 0ull);  // free for the next launch
                     *last_flag = is_last;
                 }
                 asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -575,14 +597,68 @@ void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int
     if (g < 1) g = 1;
     *grid = (int)g;
     *ws_bytes = (size_t)g * 2 * (size_t)skinny_mp(M) * (size_t)nt * sizeof(float);
-    *counter_bytes = (size_t)tiles * sizeof(int);
+    *counter_bytes = (size_t)tiles * sizeof(unsigned long long);
 }
+
+int skinny_env_nt() {
+    static const int v = [] {
+        const char* e = getenv("PAX_SKINNY_NT");
+        return e ? atoi(e) : 0;
+    }();
+    return v;
+}
+
+bool skinny_env_korder() {
+    static const bool v = [] {
+        const char* e = getenv("PAX_SKINNY_KORDER");
+        return e ? atoi(e) != 0 : false;
+    }();
+    return v;
+}
+
+// Lockstep layout when there are no more column tiles than SMs; otherwise
+// persistent stream-K, one CTA per SM.  nt_force = 128 or 256 forces the
+// persistent layout with that unit width.
+SkinnyLayout skinny_layout(long long M, long long N, long long K, int sms, int nt_force, bool korder) {
+    SkinnyLayout L;
+    int nt = nt_force;
+    L.slices = (nt == 0) ? skinny_lockstep_slices(N, K, sms) : 0;
+    if (L.slices > 0) nt = 128;
+    if (nt != 128 && nt != 256) nt = skinny_pick_nt(M, N, K, sms);
+    L.nt = nt;
+    L.korder = L.slices == 0 && korder;
+    skinny_geometry(M, N, K, sms, nt, &L.grid, &L.ws_bytes, &L.cnt_bytes);
+    if (L.slices > 0) {
+        const size_t per_cta = L.ws_bytes / (size_t)L.grid;
+        L.grid = (int)(((N + 127) / 128) * L.slices);
+        L.ws_bytes = per_cta * (size_t)L.grid;
+    }
+    return L;
+}
+
+size_t skinny_smem_bytes(long long M, int nt) {
+    const int mp = skinny_mp(M);
+    if (nt == 256)
+        return mp == 16 ? SkCfg<16, 256>::SMEM_BYTES : mp == 32 ? SkCfg<32, 256>::SMEM_BYTES
+                        : mp == 48 ? SkCfg<48, 256>::SMEM_BYTES : SkCfg<64, 256>::SMEM_BYTES;
+    return mp == 16 ? SkCfg<16, 128>::SMEM_BYTES : mp == 32 ? SkCfg<32, 128>::SMEM_BYTES
+                    : mp == 48 ? SkCfg<48, 128>::SMEM_BYTES : SkCfg<64, 128>::SMEM_BYTES;
+}
+
+// Epoch of the next launch that uses arrival counters (never 0).
+static std::atomic<unsigned int> g_skinny_epoch{0};
+static unsigned int next_epoch() {
+    unsigned int e = ++g_skinny_epoch;
+    while (e == 0) e = ++g_skinny_epoch;
+    return e;
+}
+unsigned int skinny_last_epoch() { return g_skinny_epoch.load(); }
 
 int skinny_rotation_group();
 
 template <int MP, int NT>
 static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, bool korder, float* ws,
-                                       int* counters, cudaStream_t stream) {
+                                       unsigned long long* counters, cudaStream_t stream) {
     using Cfg = SkCfg<MP, NT>;
     CUtensorMap tA, tB;
     const bool batched = pr.batch > 1;
@@ -607,6 +683,7 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
     p.b_early = (pr.b_const && pdl_enabled()) ? 1 : 0;
     p.ws = ws;
     p.counters = counters;
+    p.epoch = next_epoch();
     p.c16 = pr.c_f16 ? static_cast<__half*>(pr.C) : nullptr;
     p.c32 = pr.c_f16 ? nullptr : static_cast<float*>(pr.C);
     p.ldc = pr.ldc;
@@ -645,8 +722,8 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
 }
 
 template <int NT>
-static pax_status_t launch_skinny_nt(const Problem& p, int grid, int slices, bool korder, float* ws, int* counters,
-                                     cudaStream_t stream) {
+static pax_status_t launch_skinny_nt(const Problem& p, int grid, int slices, bool korder, float* ws,
+                                     unsigned long long* counters, cudaStream_t stream) {
     switch (skinny_mp(p.M)) {
         case 16: return launch_skinny_impl<16, NT>(p, grid, slices, korder, ws, counters, stream);
         case 32: return launch_skinny_impl<32, NT>(p, grid, slices, korder, ws, counters, stream);
@@ -669,8 +746,8 @@ int skinny_rotation_group() {
 // nt: 128 or 256 output columns per unit.  slices > 0: lockstep layout (nt
 // 128, grid = tiles x slices); 0: persistent stream-K over `grid` CTAs,
 // segments in k order when korder is set.
-pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, int* counters, cudaStream_t stream,
-                              int slices, bool korder) {
+pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, unsigned long long* counters,
+                              cudaStream_t stream, int slices, bool korder) {
     if (p.M < 1 || p.M > kSkinnyMaxM || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
     if (slices > 0) return launch_skinny_nt<128>(p, grid, slices, false, ws, counters, stream);
     if (nt == 256) return launch_skinny_nt<256>(p, grid, 0, korder, ws, counters, stream);
@@ -719,21 +796,63 @@ int read_clear_device_error_skinny() {
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
 static __device__ __align__(256) unsigned char g_skinny_scratch[kNoAllocScratchBytes];
 
-// Device address of g_skinny_scratch, looked up once per device (the host
-// symbol is only a handle; passing it to a kernel would be wrong).
-constexpr int kNoAllocMaxDevices = 64;
+// Device address of g_skinny_scratch, looked up once per device and CUDA
+// context (the host symbol is only a handle; passing it to a kernel would be
+// wrong).  The entry is keyed by the context as well as the device: after
+// the primary context is reset or released and created again, the module
+// may load at another address, and the next call looks the address up
+// again.  pax_shutdown forgets every entry.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+static CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(f);
+    });
+    return fn;
+}
+
+struct ScratchEntry {
+    int dev;
+    CUcontext ctx;
+    void* addr;
+};
 static std::mutex g_scratch_mu;
-static void* g_scratch_addr[kNoAllocMaxDevices];
+static std::vector<ScratchEntry> g_scratch_addr;
 
 static pax_status_t scratch_address(int dev, void** out) {
+    CtxGetCurrentFn get = ctx_get_current();
+    CUcontext ctx = nullptr;
+    if (!get || get(&ctx) != CUDA_SUCCESS || ctx == nullptr) return PAX_ERR_CUDA;
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
-        void* ptr = nullptr;
-        if (cudaGetSymbolAddress(&ptr, g_skinny_scratch) != cudaSuccess || ptr == nullptr) return PAX_ERR_CUDA;
-        g_scratch_addr[dev] = ptr;
+    for (const ScratchEntry& e : g_scratch_addr)
+        if (e.dev == dev && e.ctx == ctx) {
+            *out = e.addr;
+            return PAX_OK;
+        }
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_skinny_scratch) != cudaSuccess || ptr == nullptr) {
+        cudaGetLastError();
+        return PAX_ERR_CUDA;
     }
-    *out = g_scratch_addr[dev];
+    // A context this device no longer uses cannot come back: drop its entry.
+    for (size_t i = 0; i < g_scratch_addr.size(); ++i)
+        if (g_scratch_addr[i].dev == dev) {
+            g_scratch_addr.erase(g_scratch_addr.begin() + (long)i);
+            break;
+        }
+    g_scratch_addr.push_back({dev, ctx, ptr});
+    *out = ptr;
     return PAX_OK;
+}
+
+void skinny_forget_scratch() {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    g_scratch_addr.clear();
 }
 
 }  // namespace pax
@@ -751,8 +870,6 @@ extern "C" pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cud
     if (p.M == 0 || p.N == 0) return report_status(PAX_OK, "");
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return report_status(PAX_ERR_CUDA, "pax_gemm_skinny_noalloc: no device");
-    if (dev < 0 || dev >= kNoAllocMaxDevices)
-        return report_status(PAX_ERR_UNSUPPORTED, "pax_gemm_skinny_noalloc: device index above 63");
     int major = 0, sms = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -760,15 +877,15 @@ extern "C" pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cud
     if (p.M > kSkinnyMaxM || !tma_compatible(p))
         return report_status(PAX_ERR_UNSUPPORTED,
                              "pax_gemm_skinny_noalloc: needs 1 <= m <= 64, k >= 1 and 16-byte aligned rows");
-    int grid;
-    size_t ws_bytes, cnt_bytes;
-    skinny_geometry(p.M, p.N, p.K, sms, 128, &grid, &ws_bytes, &cnt_bytes);
-    const size_t cnt_pad = (cnt_bytes + 255) & ~size_t(255);
-    if (cnt_pad + ws_bytes > kNoAllocScratchBytes) {
+    // The layout pax_gemm_ex would run (lockstep for up to one column tile
+    // per SM, else stream-K), so that both entry points take the same time.
+    const SkinnyLayout L = skinny_layout(p.M, p.N, p.K, sms, skinny_env_nt(), skinny_env_korder());
+    const size_t cnt_pad = (L.cnt_bytes + 255) & ~size_t(255);
+    if (cnt_pad + L.ws_bytes > kNoAllocScratchBytes) {
         char msg[160];
         snprintf(msg, sizeof msg,
                  "pax_gemm_skinny_noalloc: problem needs %zu bytes of scratch, above the fixed %zu-byte limit",
-                 cnt_pad + ws_bytes, kNoAllocScratchBytes);
+                 cnt_pad + L.ws_bytes, kNoAllocScratchBytes);
         return report_status(PAX_ERR_UNSUPPORTED, msg);
     }
     void* scratch = nullptr;
@@ -778,8 +895,8 @@ extern "C" pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cud
     // start at zero.
     if (cudaMemsetAsync(scratch, 0, cnt_pad, stream) != cudaSuccess)
         return report_status(PAX_ERR_CUDA, "pax_gemm_skinny_noalloc: counter reset failed");
-    st = launch_skinny_ws(p, 128, grid, reinterpret_cast<float*>(static_cast<char*>(scratch) + cnt_pad),
-                          static_cast<int*>(scratch), stream);
+    st = launch_skinny_ws(p, L.nt, L.grid, reinterpret_cast<float*>(static_cast<char*>(scratch) + cnt_pad),
+                          static_cast<unsigned long long*>(scratch), stream, L.slices, L.korder);
     if (st != PAX_OK) return report_status(st, "pax_gemm_skinny_noalloc: launch failed");
     return report_status(PAX_OK, "");
 }

@@ -18,6 +18,7 @@
 #include <map>
 #include <cuda.h>
 #include <mutex>
+#include <thread>
 #include <vector>
 #include <utility>
 
@@ -100,25 +101,45 @@ static Problem batch_item(const Problem& p, long long b) {
 }
 
 // --------------------------------------------------------- workspaces
-// Split-K scratch of the skinny kernel, one buffer per (device, stream) so
-// that launches on different streams never share one.  Layout:
-// [per-tile counters: cnt_cap bytes][partial sums: ws_cap bytes].  The
-// counters must be zero when a launch starts; the kernel returns every
-// counter it used to zero, and the counter region never moves or shrinks
-// while the buffer lives, so zero counters stay zero across calls of any
-// shape.  Growing either region reallocates and zeroes the whole buffer.
+// Split-K scratch of the skinny kernel, one buffer per stream so that
+// launches on different streams never share one.  Layout:
+// [per-tile arrival counters: cnt_cap bytes][partial sums: ws_cap bytes].
+// The counters are zero when the buffer is made; the kernel frees every
+// counter it used, and one that an aborted launch left behind carries an
+// older launch epoch, which later launches ignore.  The counter region never
+// moves or shrinks while the buffer lives.  Growing either region
+// reallocates and zeroes the whole buffer.
+//
+// The key is (device, stream handle, thread).  The thread part is used only
+// for cudaStreamPerThread: that one handle value names a different stream in
+// every host thread, and two threads must not share a buffer for it.
 struct Workspace {
     void* ptr = nullptr;
     size_t cnt_cap = 0;
     size_t ws_cap = 0;
 };
+struct WsKey {
+    int dev;
+    uintptr_t stream;
+    std::thread::id thread;
+    bool operator<(const WsKey& o) const {
+        if (dev != o.dev) return dev < o.dev;
+        if (stream != o.stream) return stream < o.stream;
+        return thread < o.thread;
+    }
+};
 static std::mutex g_ws_mu;
-static std::map<std::pair<int, uintptr_t>, Workspace> g_ws;
+static std::map<WsKey, Workspace> g_ws;
 
-static pax_status_t get_workspace(int dev, cudaStream_t s, size_t cnt_need, size_t ws_need, int** counters,
-                                  float** partials) {
+static WsKey ws_key(int dev, cudaStream_t s) {
+    return {dev, reinterpret_cast<uintptr_t>(s),
+            s == cudaStreamPerThread ? std::this_thread::get_id() : std::thread::id()};
+}
+
+static pax_status_t get_workspace(int dev, cudaStream_t s, size_t cnt_need, size_t ws_need,
+                                  unsigned long long** counters, float** partials) {
     std::lock_guard<std::mutex> lk(g_ws_mu);
-    Workspace& w = g_ws[{dev, reinterpret_cast<uintptr_t>(s)}];
+    Workspace& w = g_ws[ws_key(dev, s)];
     if (w.cnt_cap < cnt_need || w.ws_cap < ws_need) {
         const size_t cnt_cap = w.cnt_cap > cnt_need ? w.cnt_cap : cnt_need;
         const size_t ws_cap = w.ws_cap > ws_need ? w.ws_cap : ws_need;
@@ -140,8 +161,23 @@ static pax_status_t get_workspace(int dev, cudaStream_t s, size_t cnt_need, size
         w.cnt_cap = cnt_cap;
         w.ws_cap = ws_cap;
     }
-    *counters = static_cast<int*>(w.ptr);
+    *counters = static_cast<unsigned long long*>(w.ptr);
     *partials = reinterpret_cast<float*>(static_cast<char*>(w.ptr) + w.cnt_cap);
+    return PAX_OK;
+}
+
+// Test hook (pax_selftest_stale_counters): write into the arrival counters
+// of this stream's workspace what a launch that gave up on a timed-out wait
+// leaves behind, one arrival under the latest launch epoch.
+static pax_status_t poison_workspace_counters(int dev, cudaStream_t s) {
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    auto it = g_ws.find(ws_key(dev, s));
+    if (it == g_ws.end() || !it->second.ptr) return PAX_ERR_INVALID;
+    const size_t n = it->second.cnt_cap / sizeof(unsigned long long);
+    std::vector<unsigned long long> v(n, ((unsigned long long)skinny_last_epoch() << 32) | 1ull);
+    if (cudaStreamSynchronize(s) != cudaSuccess ||
+        cudaMemcpy(it->second.ptr, v.data(), n * sizeof(unsigned long long), cudaMemcpyHostToDevice) != cudaSuccess)
+        return PAX_ERR_CUDA;
     return PAX_OK;
 }
 
@@ -150,7 +186,7 @@ static void free_workspaces() {
     int prev = current_device();
     for (auto& kv : g_ws) {
         if (kv.second.ptr) {
-            cudaSetDevice(kv.first.first);
+            cudaSetDevice(kv.first.dev);
             cudaDeviceSynchronize();
             cudaFree(kv.second.ptr);
         }
@@ -248,22 +284,50 @@ bool pdl_enabled() {
 
 bool tc_planning_enabled() { return env_int("PAX_TC_PLAN", 1) != 0; }
 
+// The kernel a problem runs on: `algo` as requested (AUTO: chosen here) and,
+// for the tensor-core kernel, its tile shape (128 or 256: one CTA per
+// 128 x shape tile; 2: CTA pair per 256 x 256; 4: CTA pair per 256 x 512).
+// PAX_TC_SHAPE forces a shape for AUTO; PAX_TC_BN a one-CTA tile width.
+static void choose_kernel(const Problem& p, int sms, pax_algo_t* algo, int* shape) {
+    *shape = 0;
+    if (*algo == PAX_ALGO_AUTO) {
+        *algo = select_algo(p);
+        if (*algo == PAX_ALGO_TC) {
+            *shape = tc_pick_shape(p, sms);
+            const int forced = env_int("PAX_TC_SHAPE", 0);
+            if (forced == 2 || forced == 4 || forced == 128 || forced == 256) *shape = forced;
+            if (*shape == 2 || *shape == 4) *algo = PAX_ALGO_TC2;
+        }
+    }
+    if (*algo == PAX_ALGO_TC2) {
+        if (*shape != 4) *shape = 2;
+    } else if (*algo == PAX_ALGO_TC && *shape != 128 && *shape != 256) {
+        *shape = env_int("PAX_TC_BN", 0);
+        if (*shape != 128 && *shape != 256) *shape = tc_pick_bn(p.M, p.N, sms);
+    }
+}
+
+// Dynamic shared memory of the kernel a problem runs on (0 for the CUDA-core
+// kernel, whose shared memory is static).
+static size_t kernel_smem_bytes(const Problem& p, pax_algo_t algo, int sms) {
+    int shape = 0;
+    choose_kernel(p, sms, &algo, &shape);
+    if (algo == PAX_ALGO_TC || algo == PAX_ALGO_TC2) return tc_smem_bytes(shape, p.c_f16);
+    if (algo == PAX_ALGO_SKINNY && p.M <= kSkinnyMaxM)
+        return skinny_smem_bytes(p.M, p.batch > 1 ? 128
+                                                  : skinny_layout(p.M, p.N, p.K, sms, skinny_env_nt(),
+                                                                  skinny_env_korder()).nt);
+    return 0;
+}
+
 static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
     if (p.M == 0 || p.N == 0 || p.batch == 0) return PAX_OK;
     const int dev = current_device();
     const DevInfo di = device_info(dev);
     if (di.major != 10) return fail(PAX_ERR_NO_DEVICE, "device %d is sm_%d%d; this library needs sm_100", dev,
                                     di.major, di.minor);
-    int shape = 0;  // tensor-core tile shape, when chosen here
-    if (algo == PAX_ALGO_AUTO) {
-        algo = select_algo(p);
-        if (algo == PAX_ALGO_TC) {
-            shape = tc_pick_shape(p, di.sms);
-            const int forced = env_int("PAX_TC_SHAPE", 0);
-            if (forced == 2 || forced == 4 || forced == 128 || forced == 256) shape = forced;
-            if (shape == 2 || shape == 4) algo = PAX_ALGO_TC2;
-        }
-    }
+    int shape = 0;  // tensor-core tile shape
+    choose_kernel(p, di.sms, &algo, &shape);
     pax_status_t st;
     if (p.n_replicas > 0 && algo != PAX_ALGO_TC && algo != PAX_ALGO_TC2)
         return fail(PAX_ERR_UNSUPPORTED, "replicated output needs the tensor-core path (m > %lld, 16-byte aligned rows)",
@@ -291,12 +355,6 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
         case PAX_ALGO_TC:
         case PAX_ALGO_TC2: {
             if (!tma_compatible(p)) return fail(PAX_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned rows");
-            if (algo == PAX_ALGO_TC2) {
-                if (shape != 4) shape = 2;
-            } else if (shape != 128 && shape != 256) {
-                shape = env_int("PAX_TC_BN", 0);
-                if (shape != 128 && shape != 256) shape = tc_pick_bn(p.M, p.N, di.sms);
-            }
             // The tail wave's tiles run as column halves (PAX_TC_HALVES=0
             // turns that off for comparisons).
             const TcPlan plan = tc_plan(p, shape, dev, di.sms, env_int("PAX_TC_HALVES", 1) != 0, s);
@@ -311,26 +369,14 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
             // otherwise persistent stream-K, one CTA per SM.
             // PAX_SKINNY_NT=128|256 forces the persistent layout;
             // PAX_SKINNY_KORDER=1 visits its segments in k order.
-            int nt = env_int("PAX_SKINNY_NT", 0);
-            const bool korder = env_int("PAX_SKINNY_KORDER", 0) != 0;
-            const int slices = (nt == 0) ? skinny_lockstep_slices(p.N, p.K, di.sms) : 0;
-            const bool lockstep = slices > 0;
-            if (lockstep) nt = 128;
-            if (nt != 128 && nt != 256) nt = skinny_pick_nt(p.M, p.N, p.K, di.sms);
-            int grid;
-            size_t ws_bytes, cnt_bytes;
-            skinny_geometry(p.M, p.N, p.K, di.sms, nt, &grid, &ws_bytes, &cnt_bytes);
-            if (lockstep) {
-                const size_t per_cta = ws_bytes / (size_t)grid;
-                grid = (int)(((p.N + 127) / 128) * slices);
-                ws_bytes = per_cta * (size_t)grid;
-            }
-            const size_t cnt_pad = (cnt_bytes + 255) & ~size_t(255);
-            int* counters = nullptr;
+            const SkinnyLayout L = skinny_layout(p.M, p.N, p.K, di.sms, skinny_env_nt(), skinny_env_korder());
+            const size_t cnt_pad = (L.cnt_bytes + 255) & ~size_t(255);
+            unsigned long long* counters = nullptr;
             float* partials = nullptr;
-            st = get_workspace(dev, s, cnt_pad, ws_bytes, &counters, &partials);
-            if (st != PAX_OK) return fail(st, "skinny workspace allocation failed (%zu bytes)", cnt_pad + ws_bytes);
-            st = launch_skinny_ws(p, nt, grid, partials, counters, s, slices, korder);
+            st = get_workspace(dev, s, cnt_pad, L.ws_bytes, &counters, &partials);
+            if (st != PAX_OK)
+                return fail(st, "skinny workspace allocation failed (%zu bytes)", cnt_pad + L.ws_bytes);
+            st = launch_skinny_ws(p, L.nt, L.grid, partials, counters, s, L.slices, L.korder);
             break;
         }
         case PAX_ALGO_SIMT: st = launch_simt(p, s); break;
@@ -397,6 +443,14 @@ pax_status_t pax_device_error(void) {
 void pax_shutdown(void) {
     free_workspaces();
     tc_free_plans();
+    skinny_forget_scratch();
+}
+
+pax_status_t pax_selftest_stale_counters(cudaStream_t stream) {
+    const pax_status_t st = poison_workspace_counters(current_device(), stream);
+    if (st == PAX_ERR_INVALID) return fail(st, "pax_selftest_stale_counters: no skinny workspace on this stream");
+    if (st != PAX_OK) return fail(st, "pax_selftest_stale_counters: copy failed");
+    return set_status(PAX_OK);
 }
 
 size_t pax_sizeof_buffer(void) { return sizeof(pax_buffer_t); }
@@ -553,19 +607,12 @@ int pax_gemm_pipeline_stages(const pax_gemm_desc_t* desc) {
         return 0;
     }
     // The same choices as run() makes for PAX_ALGO_AUTO.
-    const pax_algo_t a = select_algo(p);
-    if (a == PAX_ALGO_TC) {
-        int shape = tc_pick_shape(p, sms);
-        const int forced = env_int("PAX_TC_SHAPE", 0);
-        if (forced == 2 || forced == 4 || forced == 128 || forced == 256) shape = forced;
-        return tc_stages(shape);
-    }
-    if (a == PAX_ALGO_SKINNY) {
-        int nt = env_int("PAX_SKINNY_NT", 0);
-        if (nt == 0 && skinny_lockstep_slices(p.N, p.K, sms) > 0) nt = 128;
-        if (nt != 128 && nt != 256) nt = skinny_pick_nt(p.M, p.N, p.K, sms);
-        return skinny_stages(p.M, nt);
-    }
+    pax_algo_t a = PAX_ALGO_AUTO;
+    int shape = 0;
+    choose_kernel(p, sms, &a, &shape);
+    if (a == PAX_ALGO_TC || a == PAX_ALGO_TC2) return tc_stages(shape);
+    if (a == PAX_ALGO_SKINNY)
+        return skinny_stages(p.M, skinny_layout(p.M, p.N, p.K, sms, skinny_env_nt(), skinny_env_korder()).nt);
     return 0;  // CUDA-core kernel: no TMA ring
 }
 
@@ -629,9 +676,49 @@ void pax_gemm_pipeline_launch(const __half* A, const __half* B, float* C, int m,
     gemm_simple(A, B, C, m, n, k, PAX_DT_F32, PAX_EPI_NONE, 1.f, nullptr, nullptr, PAX_DT_F32, s,
                 "pax_gemm_pipeline_launch");
 }
-size_t pax_gemm_ptx_smem_bytes(void) { return tc_smem_bytes(256, false); }
-size_t pax_gemm_pipeline_smem_bytes(void) { return tc_smem_bytes(256, false); }
-size_t pax_gemm_tma_smem_bytes(void) { return tc_smem_bytes(256, false); }
+// The reference's *_smem_bytes report the shared memory of the one kernel
+// their launcher always runs (src/rtx_gemm_pipeline.cu:331-334,355-361).
+// Here the launcher picks a kernel per problem, so these report the dynamic
+// shared memory of the kernel the launcher runs for the reference's default
+// bench problem, m = n = k = 4096 with fp32 C (src/host_bridge.c:498-500),
+// on the current device (148 SMs when there is none).
+static size_t launcher_smem_bytes(pax_algo_t algo) {
+    Problem p{};
+    // Any 16-byte aligned pointers: only the shape and alignment matter.
+    alignas(16) static const __half probe_operand[8] = {};
+    alignas(16) static float probe_c[4];
+    p.A = probe_operand;
+    p.B = probe_operand;
+    p.C = probe_c;
+    p.M = p.N = p.K = 4096;
+    p.lda = p.ldb = p.ldc = 4096;
+    p.c_f16 = false;
+    p.epi.alpha = 1.f;
+    p.epi.flags = 0;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        sms = 148;
+    cudaGetLastError();
+    set_status(PAX_OK);
+    return kernel_smem_bytes(p, algo, sms);
+}
+
+size_t pax_gemm_ptx_smem_bytes(void) { return launcher_smem_bytes(PAX_ALGO_AUTO); }
+size_t pax_gemm_pipeline_smem_bytes(void) { return launcher_smem_bytes(PAX_ALGO_AUTO); }
+size_t pax_gemm_tma_smem_bytes(void) { return launcher_smem_bytes(PAX_ALGO_TC2); }
+
+size_t pax_gemm_smem_bytes(const pax_gemm_desc_t* desc) {
+    Problem p;
+    if (normalize(desc, &p) != PAX_OK) return 0;
+    set_status(PAX_OK);
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        sms = 148;
+    cudaGetLastError();
+    return kernel_smem_bytes(p, algo_of(desc), sms);
+}
 
 void pax_gemm_bias_gelu_launch(const __half* A, const __half* B, float* C, int m, int n, int k,
                                const __half* bias, cudaStream_t s) {
@@ -1060,6 +1147,8 @@ void pax_bench_all(int iters) {
         printf("%-28s  %10.4f  %10.3f\n", v.name, ms, flops / (ms * 1e9));
     }
     printf("\n");
+    // The table goes out now, not at exit, when stdout is a pipe or a file.
+    fflush(stdout);
 }
 
 }  // extern "C"

@@ -59,20 +59,39 @@ struct TcPlan {
 TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_halves, cudaStream_t stream);
 pax_status_t launch_tc(const Problem& p, const TcPlan& plan, cudaStream_t stream);
 pax_status_t launch_simt(const Problem& p, cudaStream_t stream);
-// Skinny kernel, nt (128, 256 or 512) output columns per work unit: `ws`
-// holds grid*2*MP*nt fp32 partial sums and `counters` one int per nt-column
-// tile, zero before the launch (the kernel leaves them zero again).
-// skinny_geometry gives the grid and both sizes; skinny_pick_nt the unit width.
+// Skinny kernel, nt (128 or 256) output columns per work unit: `ws` holds
+// grid*2*MP*nt fp32 partial sums and `counters` one 64-bit arrival counter
+// per nt-column tile.  Counters are zero when first used; the kernel frees
+// each one it used, and a counter an aborted launch left behind carries an
+// older launch epoch, which the next launch ignores.  skinny_geometry gives
+// the grid and both sizes; skinny_pick_nt the unit width.
 int skinny_pick_nt(long long M, long long N, long long K, int sms);
 int skinny_lockstep_slices(long long N, long long K, int sms);
 void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int* grid, size_t* ws_bytes,
                      size_t* counter_bytes);
+// The layout pax_gemm_ex runs for a skinny problem: nt, grid, K slices
+// (lockstep layout when > 0), k-ordered stream-K, and the workspace sizes.
+struct SkinnyLayout {
+    int nt = 128, grid = 1, slices = 0;
+    bool korder = false;
+    size_t ws_bytes = 0, cnt_bytes = 0;
+};
+// nt_force = 128 or 256 forces persistent stream-K with that unit width
+// (PAX_SKINNY_NT); korder visits its segments in k order (PAX_SKINNY_KORDER).
+SkinnyLayout skinny_layout(long long M, long long N, long long K, int sms, int nt_force, bool korder);
+int skinny_env_nt();
+bool skinny_env_korder();
+// Epoch of the most recent launch that was given arrival counters.
+unsigned int skinny_last_epoch();
 // slices > 0 = the lockstep layout (nt 128, `grid` = tiles x slices CTAs,
 // one per SM); its workspace is sized by skinny_geometry with that grid's
 // per-CTA share.  slices = 0: persistent stream-K, each CTA's segments in
 // k order (its later tile's head first) when korder is set.
-pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, int* counters, cudaStream_t stream,
-                              int slices = 0, bool korder = false);
+pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, unsigned long long* counters,
+                              cudaStream_t stream, int slices = 0, bool korder = false);
+// Forget the cached device address of the allocation-free path's scratch
+// array (pax_shutdown).
+void skinny_forget_scratch();
 
 // Launch the GEMM kernels with programmatic stream serialization, so that a
 // kernel's prologue overlaps the previous kernel in the stream (default on;
@@ -85,6 +104,7 @@ void tc_free_plans();
 // Shared-memory pipeline depth (TMA ring stages) of each kernel variant.
 int tc_stages(int shape);
 int skinny_stages(long long M, int nt);
+size_t skinny_smem_bytes(long long M, int nt);
 // Dynamic shared memory of the tcgen05 kernel for a tile shape / output type.
 size_t tc_smem_bytes(int shape, bool c_f16);
 // Tile width of the one-CTA shape for a problem (128 or 256).

@@ -307,9 +307,41 @@ def test_status_strings_and_version():
     assert b"sm_100a" in lib.pax_version()
 
 
+def _probe_desc(M, N, K, c_dtype=pax_b200.DType.F32, algo=Algo.AUTO, aligned=True):
+    d = GemmDesc()
+    base = 0x10000 if aligned else 0x10002  # never dereferenced: host-only queries
+    d.A, d.B, d.C = base, base, base
+    d.M, d.N, d.K = M, N, K
+    d.c_dtype = int(c_dtype)
+    d.alpha = 1.0
+    d.algo = int(algo)
+    return d
+
+
 def test_smem_queries_fit_the_part():
     for f in (lib.pax_gemm_ptx_smem_bytes, lib.pax_gemm_pipeline_smem_bytes, lib.pax_gemm_tma_smem_bytes):
         assert 0 < f() <= 232448
+
+
+def test_smem_queries_report_the_kernel_the_launcher_runs():
+    # The reference's *_smem_bytes give the dynamic shared memory of the
+    # kernel its launcher runs (src/rtx_gemm_pipeline.cu:331-334,355-361).
+    # The launchers here pick a kernel per problem; the queries answer for
+    # the reference's default bench problem, 4096^3 with fp32 C.
+    c2 = _probe_desc(4096, 4096, 4096)
+    auto = lib.pax_gemm_smem_bytes(ctypes.byref(c2))
+    assert auto > 0
+    assert lib.pax_gemm_ptx_smem_bytes() == auto
+    assert lib.pax_gemm_pipeline_smem_bytes() == auto
+    pair = lib.pax_gemm_smem_bytes(ctypes.byref(_probe_desc(4096, 4096, 4096, algo=Algo.TC2)))
+    assert lib.pax_gemm_tma_smem_bytes() == pair > 0
+    # Other kernels need other amounts; the CUDA-core kernel's is static.
+    skinny = lib.pax_gemm_smem_bytes(ctypes.byref(_probe_desc(16, 16384, 4096, c_dtype=pax_b200.DType.F16)))
+    one_cta = lib.pax_gemm_smem_bytes(ctypes.byref(_probe_desc(1024, 1024, 1024, algo=Algo.TC)))
+    assert 0 < skinny <= 232448 and 0 < one_cta <= 232448
+    assert lib.pax_gemm_smem_bytes(ctypes.byref(_probe_desc(100, 100, 7, aligned=False))) == 0
+    assert lib.pax_gemm_smem_bytes(None) == 0
+    assert lib.pax_last_error() == pax_b200.Status.INVALID
 
 
 def test_dispatch_rejects_invalid_buffers_without_gpu(capfd):
