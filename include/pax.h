@@ -388,6 +388,15 @@ pax_status_t pax_selftest_bounded_wait(cudaStream_t stream);
  * The next skinny GEMM on that stream must still be correct.  Synchronises
  * `stream`.  PAX_ERR_INVALID if the stream has no workspace yet. */
 pax_status_t pax_selftest_stale_counters(cudaStream_t stream);
+/* Test hook (new; no counterpart in the reference): sets, on the current
+ * device, the limit of the kernels' waits that a CTA may abandon, in
+ * nanoseconds (0 restores the default 2 s; values below 1000 are
+ * rejected).  With a limit of a few microseconds a real GEMM's waits run
+ * out: the kernel takes its abort path (its issued TMA loads land, its
+ * MMAs drain, TMEM is freed), records a timeout that pax_device_error()
+ * reports, and ends.  The abort path's own waits keep the 2 s limit.
+ * Synchronises the device.  For tests of the failure path only. */
+pax_status_t pax_selftest_set_wait_limit(uint64_t ns);
 
 /* Frees the device memory this library allocated on its own: the skinny
  * kernel's per-stream workspaces and the planned tile tables of the wide

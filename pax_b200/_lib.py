@@ -140,6 +140,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "pax_device_error": ([], i),
         "pax_selftest_bounded_wait": ([P], i),
         "pax_selftest_stale_counters": ([P], i),
+        "pax_selftest_set_wait_limit": ([u64], i),
         "pax_shutdown": ([], None),
         "pax_version": ([], ctypes.c_char_p),
         "pax_sizeof_buffer": ([], sz),

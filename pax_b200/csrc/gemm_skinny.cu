@@ -600,20 +600,16 @@ void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int
     *counter_bytes = (size_t)tiles * sizeof(unsigned long long);
 }
 
+// Read on every call, like the other layout switches, so that a process
+// can compare layouts.
 int skinny_env_nt() {
-    static const int v = [] {
-        const char* e = getenv("PAX_SKINNY_NT");
-        return e ? atoi(e) : 0;
-    }();
-    return v;
+    const char* e = getenv("PAX_SKINNY_NT");
+    return e ? atoi(e) : 0;
 }
 
 bool skinny_env_korder() {
-    static const bool v = [] {
-        const char* e = getenv("PAX_SKINNY_KORDER");
-        return e ? atoi(e) != 0 : false;
-    }();
-    return v;
+    const char* e = getenv("PAX_SKINNY_KORDER");
+    return e ? atoi(e) != 0 : false;
 }
 
 // Lockstep layout when there are no more column tiles than SMs; otherwise
@@ -772,6 +768,10 @@ __global__ void selftest_wait_kernel() {
 pax_status_t launch_selftest_wait(cudaStream_t stream) {
     selftest_wait_kernel<<<1, 32, 0, stream>>>();
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
+}
+
+bool set_wait_limit_skinny(unsigned long long ns) {
+    return cudaMemcpyToSymbol(g_pax_wait_limit_ns, &ns, sizeof(ns)) == cudaSuccess;
 }
 
 int read_clear_device_error_skinny() {

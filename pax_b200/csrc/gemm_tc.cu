@@ -17,6 +17,8 @@ pax_status_t launch_tc_f32(const Problem& p, const TcPlan& plan, cudaStream_t st
 int tc_pair_units_f16(int dev, int sms);
 int read_clear_device_error_tc_f16();
 int read_clear_device_error_tc_f32();
+bool set_wait_limit_tc_f16(unsigned long long ns);
+bool set_wait_limit_tc_f32(unsigned long long ns);
 
 int tc_stages(int shape) {
     return shape == 4 ? kStagesWide : shape == 2 ? kStagesPair : shape == 256 ? kStages256 : kStages128;
@@ -320,6 +322,12 @@ TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_halves,
 pax_status_t launch_tc(const Problem& p, const TcPlan& plan, cudaStream_t stream) {
     if (p.M > 0x7fffffffLL || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
     return p.c_f16 ? launch_tc_f16(p, plan, stream) : launch_tc_f32(p, plan, stream);
+}
+
+bool set_wait_limit_tc(unsigned long long ns) {
+    const bool a = set_wait_limit_tc_f16(ns);
+    const bool b = set_wait_limit_tc_f32(ns);
+    return a && b;
 }
 
 int read_clear_device_error_tc() {

@@ -744,4 +744,8 @@ static int read_clear_device_error_this_unit() {
     return v;
 }
 
+static bool set_wait_limit_this_unit(unsigned long long ns) {
+    return cudaMemcpyToSymbol(g_pax_wait_limit_ns, &ns, sizeof(ns)) == cudaSuccess;
+}
+
 }  // namespace pax

@@ -11,4 +11,6 @@ int tc_pair_units_f32(int dev, int sms) { return tc_pair_units_typed<float>(dev,
 
 int read_clear_device_error_tc_f32() { return read_clear_device_error_this_unit(); }
 
+bool set_wait_limit_tc_f32(unsigned long long ns) { return set_wait_limit_this_unit(ns); }
+
 }  // namespace pax

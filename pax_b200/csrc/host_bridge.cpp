@@ -446,6 +446,16 @@ void pax_shutdown(void) {
     skinny_forget_scratch();
 }
 
+pax_status_t pax_selftest_set_wait_limit(uint64_t ns) {
+    // 0 restores the default.  Below a microsecond every launch would give up.
+    const unsigned long long v = ns == 0 ? 2000000000ull : (unsigned long long)ns;
+    if (v < 1000ull) return fail(PAX_ERR_INVALID, "pax_selftest_set_wait_limit: %llu ns is below 1 us", v);
+    if (cudaDeviceSynchronize() != cudaSuccess) return fail(PAX_ERR_CUDA, "pax_selftest_set_wait_limit: device error");
+    if (!set_wait_limit_tc(v) || !set_wait_limit_skinny(v))
+        return fail(PAX_ERR_CUDA, "pax_selftest_set_wait_limit: copy to the device failed");
+    return set_status(PAX_OK);
+}
+
 pax_status_t pax_selftest_stale_counters(cudaStream_t stream) {
     const pax_status_t st = poison_workspace_counters(current_device(), stream);
     if (st == PAX_ERR_INVALID) return fail(st, "pax_selftest_stale_counters: no skinny workspace on this stream");

@@ -125,6 +125,10 @@ pax_status_t report_status(pax_status_t s, const char* msg);
 // the current device.
 int read_clear_device_error_tc();
 int read_clear_device_error_skinny();
+// Set the limit of the kernels' abandonable waits on the current device
+// (pax_selftest_set_wait_limit).
+bool set_wait_limit_tc(unsigned long long ns);
+bool set_wait_limit_skinny(unsigned long long ns);
 
 // Fill a device fp16 buffer with a counter-hash uniform[lo,hi) pattern
 // (bench state only).

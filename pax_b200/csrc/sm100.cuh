@@ -21,6 +21,12 @@ enum : int { PAX_DEVERR_TIMEOUT = 1 };
 
 // 2 s per wait.  A correct launch never waits longer than a few microseconds.
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;
+// Limit of the waits a CTA may abandon (those given its abort flag), per
+// translation unit and device.  It is kWaitTimeoutNs except while a test
+// shortens it (pax_selftest_set_wait_limit) to make a real GEMM's waits run
+// out.  The waits of an abort path itself (for issued TMA loads to land and
+// issued MMAs to finish) always use kWaitTimeoutNs.
+static __device__ unsigned long long g_pax_wait_limit_ns = kWaitTimeoutNs;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -84,15 +90,20 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
     return ok != 0;
 }
 
-// Slow path of mbar_wait: poll with a 2 s limit.
+// Slow path of mbar_wait: poll with a limit, 2 s unless a test shortened
+// the limit of abandonable waits.
 template <bool kCluster>
 __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
     const unsigned long long t0 = globaltimer_ns();
+    unsigned long long limit = 0;  // read at the first check, off the fast path
     for (uint32_t spin = 1;; ++spin) {
         if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
         if ((spin & 63u) == 0) {
             if (abort_flag != nullptr && *abort_flag) return false;
-            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            if (limit == 0)
+                limit = abort_flag != nullptr ? *reinterpret_cast<volatile unsigned long long*>(&g_pax_wait_limit_ns)
+                                              : (unsigned long long)kWaitTimeoutNs;
+            if (globaltimer_ns() - t0 > limit) {
                 if (abort_flag != nullptr) *abort_flag = 1;
                 atomicOr(&g_pax_device_error, PAX_DEVERR_TIMEOUT);
                 return false;

@@ -58,6 +58,7 @@ def test_header_compiles_as_c(tmp_path):
 
 C_CALLER = r"""
 /* A C99 caller of the reference's host API, linked against this library. */
+#define _POSIX_C_SOURCE 200112L
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -65,10 +66,13 @@ C_CALLER = r"""
 
 int main(void) {
     int m = 3, n = 5, k = 4, i;
-    float *a = malloc(sizeof(float) * 12), *b = malloc(sizeof(float) * 20), *c = malloc(sizeof(float) * 15);
+    float *a = NULL, *b = malloc(sizeof(float) * 20), *c = malloc(sizeof(float) * 15);
     float ref[15], acc = 0.0f;
     pax_buffer_t buf, pinned;
     pax_gemm_desc_t d;
+    /* the descriptor below promises 64-byte alignment, as the reference's
+       host allocations give */
+    if (posix_memalign((void**)&a, 64, sizeof(float) * 12) != 0) return 10;
     if (!a || !b || !c) return 10;
     /* a caller-built descriptor, as the reference's users fill one */
     memset(&buf, 0, sizeof buf);

@@ -1,4 +1,4 @@
-"""Failure detection on the GPU without a fault: a bounded wait that runs out.
+"""Failure detection on the GPU without a fault: bounded waits that run out.
 
 pax_selftest_bounded_wait launches one thread that waits, with the kernels'
 own bounded mbarrier wait, on a barrier nothing arrives on.  The wait must
@@ -36,3 +36,74 @@ def test_bounded_wait_times_out_and_context_survives(cuda, rng):
     got = run_gemm(A, B, cuda, epi="bias_gelu_tanh", bias=bias, out_dtype=np.float16)
     check(got, oracle.gemm(A, B, epi="bias_gelu_tanh", bias=bias, out_dtype=np.float16), np.float16)
     assert pax_b200.device_error() == pax_b200.Status.OK
+
+
+# ----------------------------------------------------------------- abort paths
+# The GEMM kernels' own waits run out when a test shortens the limit of the
+# waits a CTA may abandon (pax_selftest_set_wait_limit).  The kernel then
+# takes its abort path: its issued TMA loads land, its issued MMAs drain,
+# TMEM is freed, a timeout is recorded, and it ends.  Nothing faults or hangs:
+# the abort path's own waits keep the 2 s limit.  The next GEMM in the same
+# context must be correct.  The CTA-pair kernels are not driven into their
+# abort path here.
+SHORT_NS = 2000
+
+
+def _abort_run(fn):
+    lib = pax_b200.lib
+    pax_b200.device_error()  # start from a clear error word
+    assert lib.pax_selftest_set_wait_limit(SHORT_NS) == 0
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        assert lib.pax_selftest_set_wait_limit(0) == 0
+    return pax_b200.device_error()
+
+
+@pytest.mark.parametrize("shape", ["128", "256"])
+def test_tc_one_cta_kernel_abort_path(cuda, rng, monkeypatch, shape):
+    monkeypatch.setenv("PAX_TC_SHAPE", shape)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(7)
+    A = torch.randn((1024, 65536), generator=g, device=cuda).half()
+    B = torch.randn((65536, 1024), generator=g, device=cuda).half()
+    bias = torch.randn((1024,), generator=g, device=cuda).half()
+    C = torch.empty((1024, 1024), dtype=torch.float16, device=cuda)
+    st = _abort_run(lambda: pax_b200.gemm(A, B, out=C, epilogue="bias_gelu_tanh", bias=bias, algo="tc"))
+    assert st == pax_b200.Status.TIMEOUT
+    assert pax_b200.device_error() == pax_b200.Status.OK
+    del A, B
+    # The same kernel, with the default limit, is correct afterwards.
+    A2, B2 = inputs(rng, 640, 1024, 512)
+    b2 = rng.standard_normal(1024).astype(np.float16)
+    got = run_gemm(A2, B2, cuda, epi="bias_gelu_tanh", bias=b2, out_dtype=np.float16, algo="tc")
+    check(got, oracle.gemm(A2, B2, epi="bias_gelu_tanh", bias=b2, out_dtype=np.float16), np.float16)
+    assert pax_b200.device_error() == pax_b200.Status.OK
+
+
+@pytest.mark.parametrize("N", [16384, 4096])
+def test_skinny_kernel_abort_path(cuda, rng, N):
+    # N = 16384: 128 tiles, one CTA each.  N = 4096: 32 tiles with K split
+    # over 4 CTAs each, so the abort can leave split-tile arrival counters
+    # behind in this stream's workspace.
+    g = torch.Generator(device=cuda)
+    g.manual_seed(8)
+    K = 65536 if N == 4096 else 32768
+    A = torch.randn((16, K), generator=g, device=cuda).half()
+    B = (torch.randn((K, N), generator=g, device=cuda) * 0.02).half()
+    C = torch.empty((16, N), dtype=torch.float16, device=cuda)
+    st = _abort_run(lambda: pax_b200.gemm(A, B, out=C, algo="skinny"))
+    assert st == pax_b200.Status.TIMEOUT
+    assert pax_b200.device_error() == pax_b200.Status.OK
+    del A, B
+    # A split-tile problem on the same stream (same workspace) afterwards.
+    A2, B2 = inputs(rng, 16, 4096, 4096, dist="normal")
+    got = run_gemm(A2, B2, cuda, out_dtype=np.float16, algo="skinny")
+    check(got, oracle.gemm(A2, B2, out_dtype=np.float16), np.float16)
+    assert pax_b200.device_error() == pax_b200.Status.OK
+
+
+def test_wait_limit_hook_rejects_sub_microsecond_limits(cuda):
+    assert pax_b200.lib.pax_selftest_set_wait_limit(10) == pax_b200.Status.INVALID
+    assert pax_b200.lib.pax_selftest_set_wait_limit(0) == 0

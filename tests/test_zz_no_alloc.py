@@ -32,7 +32,7 @@ def _noalloc(A, B, C, epilogue="none", bias=None, residual=None):
 
 
 @pytest.mark.parametrize("M,N,K,epi", [(16, 16384, 4096, "bias"), (33, 4096, 1024, "bias_gelu_erf"),
-                                         (1, 1000, 320, "none")])
+                                         (1, 1000, 320, "none"), (16, 20480, 2048, "bias")])
 def test_noalloc_matches_workspace_entry_point_twice(cuda, rng, M, N, K, epi):
     A, B = inputs(rng, M, N, K, dist="normal")
     bias = rng.standard_normal(N).astype(np.float16)
@@ -52,17 +52,19 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda, rng, M, N, K, epi):
 
 
 def test_noalloc_rejects_problems_above_its_scratch_limit(cuda, rng):
-    # m = 64 at 148 SMs needs ~9.7 MB of partial sums, above the 8 MiB array.
-    A, B = inputs(rng, 64, 4096, 4096, dist="normal")
+    # m = 64, n = 20480 at 148 SMs: 160 column tiles, more than SMs, so the
+    # stream-K layout (256-column units); its 148 CTAs need
+    # 148 x 2 x 64 x 256 x 4 B = 19 MB of partial sums, above the 8 MiB array.
+    A, B = inputs(rng, 64, 20480, 4096, dist="normal")
     tA, tB = to_dev(A, cuda), to_dev(B, cuda)
-    C = torch.zeros((64, 4096), dtype=torch.float16, device=cuda)
+    C = torch.zeros((64, 20480), dtype=torch.float16, device=cuda)
     if torch.cuda.get_device_properties(0).multi_processor_count < 140:
         pytest.skip("scratch need depends on the SM count")
     st = _noalloc(tA, tB, C)
     assert st == pax_b200.Status.UNSUPPORTED
     torch.cuda.synchronize()
     assert (C == 0).all()  # nothing was launched
-    big = torch.zeros((80, 4096), dtype=torch.float16, device=cuda)
+    big = torch.zeros((80, 20480), dtype=torch.float16, device=cuda)
     A80 = torch.zeros((80, 4096), dtype=torch.float16, device=cuda)
     assert _noalloc(A80, tB, big) == pax_b200.Status.UNSUPPORTED  # m > 64
 
