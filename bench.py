@@ -545,6 +545,8 @@ def timed_steps(step, steps, warmup, flush, dev, world, local):
     if clk is not None:
         # Cycles per step at the median SM clock of the timed region.
         clk["kcycles_per_step_at_median"] = mean * clk["sm_mhz"]
+        clk["step_ms"] = {"first": [round(x, 5) for x in ms[:5]], "last": [round(x, 5) for x in ms[-5:]],
+                          "median": statistics.median(ms), "min": min(ms), "max": max(ms)}
     return {"ms": ms, "mean": mean, "max_over_ranks": float(t.item()), "clocks": clk}
 
 
@@ -623,7 +625,8 @@ def noalloc_record(A, B, bias, C, cfg, alg_bytes, hbm, flush, dev, steps, warmup
     r = timed_steps(step, steps, warmup, flush, dev, 1, dev.index)
     gbs = alg_bytes / (r["mean"] * 1e-3) / 1e9
     return {"us_per_gemm": r["mean"] * 1e3, "achieved": gbs, "frac": gbs / hbm,
-            "launches_per_call": 2, "note": "a 256-byte counter clear (cudaMemsetAsync) and the GEMM"}
+            "note": "one GEMM launch; a counter clear (cudaMemsetAsync) precedes it only in layouts that split tiles, "
+                    "which C4's lockstep layout (one CTA per 128-column tile) does not"}
 
 
 def split_record(args, dev, flush, peak, world, rank, local, steps, warmup, gather_too):

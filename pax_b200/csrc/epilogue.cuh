@@ -82,9 +82,10 @@ struct ResChunk {
     uint4 u[V];
 };
 
+// `pol` is the L2 policy of the loads: the residual is read once.
 template <int n, int RES>
 __device__ __forceinline__ void res_prefetch(ResChunk<n, RES>& rc, long long row, long long col0, long long M,
-                                             long long N, const EpiParams& ep) {
+                                             long long N, const EpiParams& ep, uint64_t pol) {
     if constexpr (RES == 0) {
         return;
     } else {
@@ -96,7 +97,7 @@ __device__ __forceinline__ void res_prefetch(ResChunk<n, RES>& rc, long long row
             const float* rp = static_cast<const float*>(ep.residual) + row * ep.ld_res + col0;
             if (full) {
 #pragma unroll
-                for (int i = 0; i < n / 4; ++i) rc.u[i] = ld_nc_v4(rp + 4 * i);
+                for (int i = 0; i < n / 4; ++i) rc.u[i] = ld_nc_v4_hint(rp + 4 * i, pol);
             } else {
 #pragma unroll
                 for (int i = 0; i < n / 4; ++i) {
@@ -111,7 +112,7 @@ __device__ __forceinline__ void res_prefetch(ResChunk<n, RES>& rc, long long row
             const __half* rp = static_cast<const __half*>(ep.residual) + row * ep.ld_res + col0;
             if (full) {
 #pragma unroll
-                for (int i = 0; i < n / 8; ++i) rc.u[i] = ld_nc_v4(rp + 8 * i);
+                for (int i = 0; i < n / 8; ++i) rc.u[i] = ld_nc_v4_hint(rp + 8 * i, pol);
             } else {
 #pragma unroll
                 for (int i = 0; i < n / 8; ++i) {

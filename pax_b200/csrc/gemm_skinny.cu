@@ -213,8 +213,17 @@ __global__ void __launch_bounds__(192, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int KB = p.kblocks;
-    const int rot = sk_rotation(p);  // first k-block of this CTA's k loop
+
+    // Producer state (thread 0, the TMA producer of warp 0), kept across the
+    // barrier below: the producer issues the first ring of loads before it,
+    // right after initialising the barriers, so that the first bytes are on
+    // their way while the other warps still set up.
+    int p_stage = 0;
+    uint32_t p_phase = 0, p_issued = 0, p_last_parity = 0;
+    long long p_cur = 0;
+    SkSeg p_sg = {0, 0, 1, 0};
+    bool p_has_seg = false;
+    int p_j = 0;  // next k-block of the current segment
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -228,10 +237,52 @@ __global__ void __launch_bounds__(192, 1)
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_mbar_init();
-    }
-    if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        const int rot0 = sk_rotation(p);
+        p_cur = sk_cursor0(p);
+        p_has_seg = sk_next_seg(p, p_cur, p_sg);
+        // The first segment's first ring of k-blocks: every slot is free.
+        const int nfill = p_has_seg ? (p_sg.nk < STAGES ? p_sg.nk : STAGES) : 0;
+        const int bz0 = p_sg.tile / p.num_tiles, tl0 = p_sg.tile - bz0 * p.num_tiles;
+        const int za0 = p.za ? bz0 : 0, zb0 = p.zb ? bz0 : 0;
+        if (p.b_early) {
+            // Before waiting for the previous grid (the caller promised it
+            // does not write B), B of those k-blocks is copied into their
+            // slots now.  Each slot's barrier expects B's bytes without
+            // arriving, so it completes only after A, issued after the wait,
+            // lands too.
+            for (int jj = 0; jj < nfill; ++jj) {
+                const int kb = sk_kblock(p, p_sg, jj, rot0);
+                const uint32_t fb = full0 + 8u * jj;
+                mbar_expect_tx(fb, Cfg::B_BYTES);
+                const uint32_t bdst = smem_u32(sB + jj * Cfg::B_BYTES);
+#pragma unroll
+                for (int b = 0; b < NT / 64; ++b)
+                    tma_load_3d(bdst + b * 8192u, &tmB, fb, tl0 * NT + b * 64, kb * 64, zb0);
+            }
+        }
+        pdl_wait();  // A and B may be written by the previous grid
+        for (int jj = 0; jj < nfill; ++jj) {
+            const int kb = sk_kblock(p, p_sg, jj, rot0);
+            const uint32_t fb = full0 + 8u * jj;
+            if (p.b_early) {
+                mbar_arrive_expect_tx(fb, Cfg::A_BYTES);
+            } else {
+                mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+                const uint32_t bdst = smem_u32(sB + jj * Cfg::B_BYTES);
+                // All NT/64 boxes of this k-block together: NT*2 contiguous
+                // bytes of every k-row of B.
+#pragma unroll
+                for (int b = 0; b < NT / 64; ++b)
+                    tma_load_3d(bdst + b * 8192u, &tmB, fb, tl0 * NT + b * 64, kb * 64, zb0);
+            }
+            tma_load_3d(smem_u32(sA + jj * Cfg::A_BYTES), &tmA, fb, kb * 64, 0, za0);
+        }
+        p_issued = (1u << nfill) - 1u;  // all at phase 0
+        p_j = nfill;
+        p_stage = nfill == STAGES ? 0 : nfill;
+        p_phase = nfill == STAGES ? 1u : 0u;
     }
     if (warp == 1) {
         tmem_alloc<1>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
@@ -241,89 +292,46 @@ __global__ void __launch_bounds__(192, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    const int KB = p.kblocks;
+    const int rot = sk_rotation(p);  // first k-block of this CTA's k loop
     // A following kernel launched with programmatic serialization may start
     // its prologue now; it waits for this grid before touching memory.
     if (threadIdx.x == 0) pdl_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            uint32_t issued = 0, last_parity = 0;
+            // The rest of the loads, from where the first ring stopped.
             bool ok = true;
-            long long cur = sk_cursor0(p);
-            SkSeg sg;
-            int n_early = 0;  // leading stages whose B was issued before the wait
-            {
-                // Before waiting for the previous grid, this CTA's first
-                // k-blocks of B (the first segment's first ring-full):
-                //   b_early (the caller promised B is not written by that
-                //   grid): copied into the ring's stages now.  Each stage's
-                //   barrier expects B's bytes without arriving, so it
-                //   completes only after A, issued after the wait, lands too.
-                //   Otherwise: pulled into L2 only.  A prefetch warms the
-                //   cache and cannot observe data that grid is still
-                //   writing; every shared-memory load then follows the wait.
-                long long c0 = cur;
-                SkSeg s0;
-                if (sk_next_seg(p, c0, s0)) {
-                    const int n0 = s0.nk < STAGES ? s0.nk : STAGES;
-                    const int bz0 = s0.tile / p.num_tiles, tl0 = s0.tile - bz0 * p.num_tiles;
-                    const int zb0 = p.zb ? bz0 : 0;
-                    for (int j = 0; j < n0; ++j) {
-                        const int kb = sk_kblock(p, s0, j, rot);
-                        if (p.b_early) {
-                            const uint32_t fb = full0 + 8u * j;
-                            mbar_expect_tx(fb, Cfg::B_BYTES);
-                            const uint32_t bdst = smem_u32(sB + j * Cfg::B_BYTES);
-#pragma unroll
-                            for (int b = 0; b < NT / 64; ++b)
-                                tma_load_3d(bdst + b * 8192u, &tmB, fb, tl0 * NT + b * 64, kb * 64, zb0);
-                        } else {
-#pragma unroll
-                            for (int b = 0; b < NT / 64; ++b)
-                                tma_prefetch_l2(&tmB, tl0 * NT + b * 64, kb * 64, zb0);
-                        }
-                    }
-                    if (p.b_early) n_early = n0;
-                }
-            }
-            pdl_wait();
-            int i_kb = 0;  // k-blocks issued so far by this CTA
-            while (ok && sk_next_seg(p, cur, sg))
-            for (int j = 0; j < sg.nk; ++j, ++i_kb) {
-                const int bz = sg.tile / p.num_tiles, tile = sg.tile - bz * p.num_tiles;
+            while (ok && p_has_seg) {
+                const int bz = p_sg.tile / p.num_tiles, tile = p_sg.tile - bz * p.num_tiles;
                 const int za = p.za ? bz : 0, zb = p.zb ? bz : 0;
-                const int kb = sk_kblock(p, sg, j, rot);
-                if (!mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t fb = full0 + 8u * stage;
-                if (i_kb < n_early) {
-                    // B of this stage is already on its way (issued above,
-                    // same stage, same k-block): arrive with A's bytes only.
-                    mbar_arrive_expect_tx(fb, Cfg::A_BYTES);
-                } else {
+                for (; p_j < p_sg.nk; ++p_j) {
+                    const int kb = sk_kblock(p, p_sg, p_j, rot);
+                    if (!mbar_wait(empty0 + 8u * p_stage, p_phase ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = full0 + 8u * p_stage;
                     mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
-                    const uint32_t bdst = smem_u32(sB + stage * Cfg::B_BYTES);
-                    // All NT/64 boxes of this k-block together: NT*2
-                    // contiguous bytes of every k-row of B.
+                    const uint32_t bdst = smem_u32(sB + p_stage * Cfg::B_BYTES);
 #pragma unroll
                     for (int b = 0; b < NT / 64; ++b)
                         tma_load_3d(bdst + b * 8192u, &tmB, fb, tile * NT + b * 64, kb * 64, zb);
+                    tma_load_3d(smem_u32(sA + p_stage * Cfg::A_BYTES), &tmA, fb, kb * 64, 0, za);
+                    p_issued |= 1u << p_stage;
+                    p_last_parity = (p_last_parity & ~(1u << p_stage)) | (p_phase << p_stage);
+                    if (++p_stage == STAGES) {
+                        p_stage = 0;
+                        p_phase ^= 1u;
+                    }
                 }
-                tma_load_3d(smem_u32(sA + stage * Cfg::A_BYTES), &tmA, fb, kb * 64, 0, za);
-                issued |= 1u << stage;
-                last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
+                if (!ok) break;
+                p_has_seg = sk_next_seg(p, p_cur, p_sg);
+                p_j = 0;
             }
             if (!ok)
                 for (int s = 0; s < STAGES; ++s)
-                    if (issued & (1u << s)) mbar_wait(full0 + 8u * s, (last_parity >> s) & 1u, nullptr);
+                    if (p_issued & (1u << s)) mbar_wait(full0 + 8u * s, (p_last_parity >> s) & 1u, nullptr);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -386,6 +394,18 @@ __global__ void __launch_bounds__(192, 1)
         SkSeg sg;
         while (sk_next_seg(p, cur, sg)) {
             const int tile = sg.tile;  // global tile (item * num_tiles + tile) in batched launches
+            // This thread's bias values, loaded before the accumulator wait so
+            // that their latency is hidden behind it.
+            float bpre[NSUB];
+            {
+                const int bz = tile / p.num_tiles, tl = tile - bz * p.num_tiles;
+                const __half* bias = (p.epi.flags & EPI_BIAS) ? p.epi.bias + (long long)bz * p.sbias : nullptr;
+#pragma unroll
+                for (int sb = 0; sb < NSUB; ++sb) {
+                    const long long n = (long long)tl * NT + sb * 128 + n_local;
+                    bpre[sb] = (bias != nullptr && n < p.N) ? __half2float(bias[n]) : 0.f;
+                }
+            }
             // All four epilogue warps take the same branch (they meet at named
             // barriers below), so the wait outcome is AND-reduced across them.
             const bool ok = named_barrier_and<1, 128>(mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag));
@@ -472,7 +492,6 @@ __global__ void __launch_bounds__(192, 1)
                 const int flags = p.epi.flags;
                 // Batch item of this tile (0 unless batched) and its operands.
                 const int bz = tile / p.num_tiles, tl = tile - bz * p.num_tiles;
-                const __half* bias = p.epi.bias ? p.epi.bias + (long long)bz * p.sbias : nullptr;
                 const long long res_off = (long long)bz * p.sres;
                 __half* c16 = p.c16 ? p.c16 + (long long)bz * p.sc : nullptr;
                 float* c32 = p.c32 ? p.c32 + (long long)bz * p.sc : nullptr;
@@ -487,7 +506,7 @@ __global__ void __launch_bounds__(192, 1)
                 for (int sb = 0; sb < NSUB; ++sb) {
                     const long long n = (long long)tl * NT + sb * 128 + n_local;
                     if (n >= p.N) continue;
-                    const float b = has_bias ? __half2float(bias[n]) : 0.f;
+                    const float b = bpre[sb];
                     if (lean) {
 #pragma unroll
                         for (int m = 0; m < MP; ++m)
@@ -892,8 +911,10 @@ extern "C" pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cud
     if (scratch_address(dev, &scratch) != PAX_OK)
         return report_status(PAX_ERR_CUDA, "pax_gemm_skinny_noalloc: cudaGetSymbolAddress failed");
     // The array keeps whatever the previous call left; the counters must
-    // start at zero.
-    if (cudaMemsetAsync(scratch, 0, cnt_pad, stream) != cudaSuccess)
+    // start at zero.  The lockstep layout with one K slice per tile splits no
+    // tile and uses no counters, so it needs no clear.
+    const bool uses_counters = !(L.slices == 1);
+    if (uses_counters && cudaMemsetAsync(scratch, 0, cnt_pad, stream) != cudaSuccess)
         return report_status(PAX_ERR_CUDA, "pax_gemm_skinny_noalloc: counter reset failed");
     st = launch_skinny_ws(p, L.nt, L.grid, reinterpret_cast<float*>(static_cast<char*>(scratch) + cnt_pad),
                           static_cast<unsigned long long*>(scratch), stream, L.slices, L.korder);

@@ -49,6 +49,7 @@ struct TcParams {
     int M, N, K;
     int tiles_m, tiles_n, num_tiles;
     int group_m;  // output tiles are visited in column-major groups of group_m tile rows
+    int c_evict_first;  // store C with an L2 evict-first policy (C much larger than L2)
     // Work items: tiles [0, full_items) whole, then the last tail_tiles tiles
     // (the tail wave) as two column halves each, so
     // num_items = full_items + 2 * tail_tiles.
@@ -428,6 +429,8 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         const int q = warp & 3;          // TMEM lane quarter this warp may read
         const int wh = (warp - 2) >> 2;  // which half of the item's columns
         uint8_t* sbuf = sStg + (warp - 2) * Cfg::STG_BYTES;
+        // Residual and (when much larger than L2) C pass through L2 once.
+        const uint64_t pol_stream = l2_evict_first_policy();
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int k = k_begin; k < k_end; k += k_step) {
@@ -448,7 +451,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             // waiting for it: this warp's bias and the first residual chunk.
             const uint4 bias8 = bias_tile_load(tcol0, wcols, lane, p.N, ep);
             ResChunk<32, RES> rc;
-            if (wcols > 0) res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, ep);
+            if (wcols > 0) res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, ep, pol_stream);
             bool ok = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
@@ -490,7 +493,8 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     // The residual registers are free again: start the next
                     // sub-chunk's loads, which then overlap the GeLU math below.
                     if constexpr (RES != 0) {
-                        if (c + 32 < nch * EC) res_prefetch<32, RES>(rc, row, tcol0 + c + 32, p.M, p.N, ep);
+                        if (c + 32 < nch * EC)
+                            res_prefetch<32, RES>(rc, row, tcol0 + c + 32, p.M, p.N, ep, pol_stream);
                     }
                     epi_gelu<32, GELU>(v);
 #pragma unroll
@@ -515,7 +519,10 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_3d(&tmC, smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz);
+                    if (p.c_evict_first)
+                        tma_store_3d_hint(&tmC, smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz, pol_stream);
+                    else
+                        tma_store_3d(&tmC, smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz);
                     for (int d = 0; d < reps.n; ++d)
                         tma_store_3d(&reps.map[d], smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz);
                     bulk_commit();
@@ -644,6 +651,15 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     // measured best for 256 x 512 (C5: 1182 vs 1049 TF/s with 8) and for
     // 128-row one-CTA tiles (U = 148).
     p.group_m = (PAIR && !Cfg::WIDE) ? 8 : 16;
+    if (const char* g = getenv("PAX_TC_GROUP")) {
+        const int v = atoi(g);
+        if (v >= 1 && v <= 1024) p.group_m = v;
+    }
+    // C written once and much larger than L2 would push A and B out of it:
+    // store it with an evict-first policy (PAX_TC_C_EVICT=0/1 forces).
+    const long long c_bytes = pr.M * pr.N * (long long)ce * pr.batch;
+    p.c_evict_first = c_bytes > (64LL << 20) ? 1 : 0;
+    if (const char* e = getenv("PAX_TC_C_EVICT")) p.c_evict_first = atoi(e) != 0 ? 1 : 0;
     p.full_items = plan.full_items;
     p.tail_tiles = plan.tail_tiles;
     p.num_items = plan.full_items + 2 * plan.tail_tiles;

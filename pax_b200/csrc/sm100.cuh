@@ -95,19 +95,18 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 template <bool kCluster>
 __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
     const unsigned long long t0 = globaltimer_ns();
-    unsigned long long limit = 0;  // read at the first check, off the fast path
-    for (uint32_t spin = 1;; ++spin) {
+    unsigned long long limit = 0;  // read after the first unsuccessful try
+    // try_wait itself suspends the thread for a while (until the phase
+    // completes or a hardware time limit passes), so the abort flag and the
+    // clock are checked after every unsuccessful try.
+    for (;;) {
         if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
-        if ((spin & 63u) == 0) {
-            if (abort_flag != nullptr && *abort_flag) return false;
-            if (limit == 0)
-                limit = abort_flag != nullptr ? *reinterpret_cast<volatile unsigned long long*>(&g_pax_wait_limit_ns)
-                                              : (unsigned long long)kWaitTimeoutNs;
-            if (globaltimer_ns() - t0 > limit) {
-                if (abort_flag != nullptr) *abort_flag = 1;
-                atomicOr(&g_pax_device_error, PAX_DEVERR_TIMEOUT);
-                return false;
-            }
+        if (abort_flag != nullptr && *abort_flag) return false;
+        if (limit == 0) limit = abort_flag != nullptr ? g_pax_wait_limit_ns : (unsigned long long)kWaitTimeoutNs;
+        if (globaltimer_ns() - t0 > limit) {
+            if (abort_flag != nullptr) *abort_flag = 1;
+            atomicOr(&g_pax_device_error, PAX_DEVERR_TIMEOUT);
+            return false;
         }
     }
 }
@@ -177,6 +176,15 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
         "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
             reinterpret_cast<uint64_t>(map)),
         "r"(src), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+// As tma_store_3d, with an L2 cache policy for the written lines.
+__device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y,
+                                                  int32_t z, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%2, %3, %4}], [%1], %5;" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(src), "r"(x), "r"(y), "r"(z), "l"(pol)
         : "memory");
 }
 // L2 prefetch of one 2-D box (a hint: no data reaches the SM).
@@ -388,6 +396,21 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, bool a_mn_ma
 }
 
 // ----------------------------------------------------------- misc memory
+// L2 policy that marks lines as first to evict: for data read or written
+// once (a residual, an output much larger than L2), so that it does not push
+// the reused operand tiles out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint4 ld_nc_v4_hint(const void* p, uint64_t pol) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p), "l"(pol));
+    return r;
+}
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
     uint4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
