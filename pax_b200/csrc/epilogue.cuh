@@ -15,7 +15,7 @@
 //   exact form (no reference code; the definition PAX/GEMM.lean:150-152
 //   bounds the tanh form against): 0.5 x (1 + erf(x / sqrt 2))
 // tanh: CUDA's tanhf, or the hardware tanh.approx.f32 for fp16 results;
-// erf: CUDA's erff.
+// erf: Abramowitz & Stegun 7.1.28 (see gelu_erf).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -46,8 +46,35 @@ __device__ __forceinline__ float gelu_tanh_hw(float x) {
     return 0.5f * x * (1.0f + tanh_hw(k_alpha * (x + k_beta * x * x * x)));
 }
 
+// Exact-form GeLU, 0.5 x (1 + erf(x / sqrt 2)), with erf from Abramowitz &
+// Stegun, Handbook of Mathematical Functions (1964), formula 7.1.28
+// (Hastings' rational approximation): for w >= 0
+//   erf(w) = 1 - q,  q = (1 + a1 w + a2 w^2 + ... + a6 w^6)^-16,
+// |error| <= 3e-7, and erf(-w) = -erf(w).  So 1 + erf(z) is 2 - q for
+// z >= 0 and q itself for z < 0, with no cancellation in the negative tail.
+// One reciprocal on the special-function unit and about a dozen FMA-pipe
+// operations per value; the fp32 result is within about 1e-6 of the exact
+// GeLU (checked against double-precision erf over |x| <= 20).
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ float gelu_erf(float x) {
-    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+    const float z = x * 0.70710678118654752f;
+    const float w = fabsf(z);
+    float p = fmaf(w, 4.30638e-5f, 2.765672e-4f);
+    p = fmaf(p, w, 1.520143e-4f);
+    p = fmaf(p, w, 9.2705272e-3f);
+    p = fmaf(p, w, 4.22820123e-2f);
+    p = fmaf(p, w, 7.05230784e-2f);
+    p = fmaf(p, w, 1.0f);
+    p *= p;
+    p *= p;
+    p *= p;
+    p *= p;                         // p^16 (inf for |z| above about 19: q = 0)
+    const float q = rcp_approx(p);  // 1 - erf(w)
+    return 0.5f * x * (z >= 0.f ? 2.0f - q : q);
 }
 
 
@@ -83,9 +110,15 @@ struct ResChunk {
 };
 
 // `pol` is the L2 policy of the loads: the residual is read once.
+__device__ __forceinline__ uint4 res_ld(const void* p, uint64_t pol, int mode) {
+    if (mode == 0) return ld_nc_v4(p);
+    if (mode == 1) return ld_nc_v4_hint(p, pol);
+    if (mode == 2) return ld_nc_v4_l1_hint(p, pol);
+    return ld_nc_v4_l1(p);
+}
 template <int n, int RES>
 __device__ __forceinline__ void res_prefetch(ResChunk<n, RES>& rc, long long row, long long col0, long long M,
-                                             long long N, const EpiParams& ep, uint64_t pol) {
+                                             long long N, const EpiParams& ep, uint64_t pol, int mode = 1) {
     if constexpr (RES == 0) {
         return;
     } else {
@@ -97,7 +130,7 @@ __device__ __forceinline__ void res_prefetch(ResChunk<n, RES>& rc, long long row
             const float* rp = static_cast<const float*>(ep.residual) + row * ep.ld_res + col0;
             if (full) {
 #pragma unroll
-                for (int i = 0; i < n / 4; ++i) rc.u[i] = ld_nc_v4_hint(rp + 4 * i, pol);
+                for (int i = 0; i < n / 4; ++i) rc.u[i] = res_ld(rp + 4 * i, pol, mode);
             } else {
 #pragma unroll
                 for (int i = 0; i < n / 4; ++i) {
@@ -112,7 +145,7 @@ __device__ __forceinline__ void res_prefetch(ResChunk<n, RES>& rc, long long row
             const __half* rp = static_cast<const __half*>(ep.residual) + row * ep.ld_res + col0;
             if (full) {
 #pragma unroll
-                for (int i = 0; i < n / 8; ++i) rc.u[i] = ld_nc_v4_hint(rp + 8 * i, pol);
+                for (int i = 0; i < n / 8; ++i) rc.u[i] = res_ld(rp + 8 * i, pol, mode);
             } else {
 #pragma unroll
                 for (int i = 0; i < n / 8; ++i) {
@@ -153,7 +186,7 @@ __device__ __forceinline__ uint4 bias_tile_load(long long tile_col0, int tile_co
 // Epilogue of one row chunk of n columns starting at tile column `tc` (a
 // multiple of 8), in two phases so the caller can refill `rc` in between:
 //   epi_linear: v = alpha*v (+ bias[j]) (+ R[i][j])
-//   epi_gelu:   v = GeLU(v)     GELU: 0 none, 1 tanh (tanhf), 2 erf (erff), 3 tanh (tanh.approx)
+//   epi_gelu:   v = GeLU(v)     GELU: 0 none, 1 tanh (tanhf), 2 erf (gelu_erf), 3 tanh (tanh.approx)
 // `bias8` is this lane's bias_tile_load value.
 template <int n, int RES>
 __device__ __forceinline__ void epi_linear(float (&v)[n], const ResChunk<n, RES>& rc, uint4 bias8, int tc,

@@ -36,7 +36,7 @@ struct SkinnyParams {
     long long work; // num_tiles * kblocks
     int grid;       // number of CTAs (<= work)
     int slices;     // lockstep layout: K slices per tile (CTA = tile * slices + slice); 0 = stream-K
-    int korder;     // stream-K only: visit the CTA's segments last to first
+    int korder;     // stream-K: the CTA's segments last to first (always set there; see sk_next_seg)
     // Lockstep layout with one slice per tile only: CTAs in groups of
     // rot_group start their k loop at different k-blocks (group g at
     // g * kblocks / groups, wrapping around), so that fewer CTAs read the same
@@ -50,13 +50,13 @@ struct SkinnyParams {
     // items share slice 0).  sc, sbias, sres: element strides between items.
     int rr, batch, za, zb;
     long long sc, sbias, sres;
-    float* ws;      // [grid][2][MP][NT] fp32 partial sums
-    // [num_tiles] arrival counters of split tiles: (launch epoch << 32) |
-    // arrivals, 0 when free.  A counter left by an earlier launch (one that
-    // gave up on a timed-out wait before its last contributor arrived) has an
-    // older epoch and is restarted, so it cannot elect the wrong last arriver.
-    unsigned long long* counters;
-    unsigned int epoch;  // this launch's epoch, never 0
+    float* ws;      // [grid][MP][NT] fp32 partial sums, one slot per CTA
+    // [grid] publication flags: CTA c sets flags[c] to this launch's epoch
+    // once its partial sum is in its slot.  A flag left by an earlier launch
+    // (finished or aborted) holds an older epoch, so nothing needs clearing
+    // between launches.
+    unsigned long long* flags;
+    unsigned long long epoch;  // this launch's epoch, never 0 (64 bits: never wraps in practice)
     __half* c16;    // exactly one of c16 / c32 is set
     float* c32;
     long long ldc;
@@ -202,7 +202,6 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(sA + STAGES * Cfg::A_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NUM_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
     const uint32_t bar0 = smem_u32(bars);
     const uint32_t full0 = bar0;
@@ -215,9 +214,12 @@ __global__ void __launch_bounds__(192, 1)
     const int lane = threadIdx.x & 31;
 
     // Producer state (thread 0, the TMA producer of warp 0), kept across the
-    // barrier below: the producer issues the first ring of loads before it,
-    // right after initialising the barriers, so that the first bytes are on
-    // their way while the other warps still set up.
+    // barrier below: the producer issues the first k-block's loads before
+    // it, right after initialising the barriers, so that the first bytes are
+    // on their way while the other warps still set up.  Only one: a whole
+    // ring's worth of loads issued at once by every CTA completes later, k-block
+    // by k-block, than loads issued as the ring drains (measured on B200:
+    // first k-block 3.6 us after kernel start with one, 6.0 us with twelve).
     int p_stage = 0;
     uint32_t p_phase = 0, p_issued = 0, p_last_parity = 0;
     long long p_cur = 0;
@@ -242,8 +244,10 @@ __global__ void __launch_bounds__(192, 1)
         const int rot0 = sk_rotation(p);
         p_cur = sk_cursor0(p);
         p_has_seg = sk_next_seg(p, p_cur, p_sg);
-        // The first segment's first ring of k-blocks: every slot is free.
-        const int nfill = p_has_seg ? (p_sg.nk < STAGES ? p_sg.nk : STAGES) : 0;
+        // The first segment's first k-block (its slot is free).  With b_early
+        // the whole first ring of B is copied before the previous grid ends,
+        // so A follows for all of it.
+        const int nfill = !p_has_seg ? 0 : p.b_early ? (p_sg.nk < STAGES ? p_sg.nk : STAGES) : 1;
         const int bz0 = p_sg.tile / p.num_tiles, tl0 = p_sg.tile - bz0 * p.num_tiles;
         const int za0 = p.za ? bz0 : 0, zb0 = p.zb ? bz0 : 0;
         if (p.b_early) {
@@ -429,10 +433,15 @@ __global__ void __launch_bounds__(192, 1)
             const bool whole = p.slices > 0 ? p.slices == 1 : (sg.kb0 == 0 && sg.nk == KB);
             bool do_out = whole;
             if (!whole) {
-                // Park the partial sum, then count contributions for this tile.
-                // Contributors: CTAs c_first..c_last; CTA c's partial for this
-                // tile is in its slot cslot(c).
-                const int slot = (p.slices > 0 || tile == first_tile) ? 0 : 1;
+                // A split tile: contributors c_first..c_last.  The last one
+                // (the tile's last K slice; in stream-K the CTA holding the
+                // tile's tail, which it computes last) adds the others'
+                // partial sums to its own, in CTA order, and writes C.  The
+                // others publish theirs: the partial sum to their slot, then
+                // their flag.  In stream-K a CTA publishes only the first
+                // segment it computes (the head of its later tile), so one
+                // slot per CTA suffices, and the tail owner finds the head
+                // long published.
                 int c_first, c_last;
                 if (p.slices > 0) {
                     c_first = tile * p.slices;
@@ -441,51 +450,44 @@ __global__ void __launch_bounds__(192, 1)
                     c_first = sk_owner((long long)tile * KB, p);
                     c_last = sk_owner((long long)(tile + 1) * KB - 1, p);
                 }
-                float* wp = p.ws + ((size_t)blockIdx.x * 2 + slot) * (size_t)(MP * NT);
-#pragma unroll
-                for (int sb = 0; sb < NSUB; ++sb)
-#pragma unroll
-                    for (int m = 0; m < MP; ++m) wp[m * NT + sb * 128 + n_local] = v[sb][m];
-                __threadfence();
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (et == 0) {
-                    unsigned long long* ctr = p.counters + tile;
-                    const unsigned long long first = ((unsigned long long)p.epoch << 32) | 1ull;
-                    unsigned long long seen = atomicCAS(ctr, 0ull, first);
-                    unsigned int arrivals = 1;
-                    while (seen != 0ull) {
-                        // Same launch: one more arrival.  Older epoch: a
-                        // leftover, restart the count.
-                        const unsigned long long want = (unsigned int)(seen >> 32) == p.epoch ? seen + 1ull : first;
-                        const unsigned long long prev = atomicCAS(ctr, seen, want);
-                        if (prev == seen) {
-                            arrivals = (unsigned int)want;
-                            break;
-                        }
-                        seen = prev;
-                    }
-                    const int is_last = (arrivals == (unsigned int)(c_last - c_first + 1)) ? 1 : 0;
-                    if (is_last) atomicExch(ctr, 0ull);  // free for the next launch
-                    *last_flag = is_last;
-                }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                do_out = (*last_flag != 0);
-                // Every epilogue thread has read the flag before it is reused.
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (do_out) {
-                    __threadfence();
+                if ((int)blockIdx.x != c_last) {
+                    float* wp = p.ws + (size_t)blockIdx.x * (size_t)(MP * NT);
 #pragma unroll
                     for (int sb = 0; sb < NSUB; ++sb)
 #pragma unroll
-                        for (int m = 0; m < MP; ++m) v[sb][m] = 0.f;
-                    for (int c = c_first; c <= c_last; ++c) {
-                        const int cs = (p.slices > 0 || (int)(sk_unit_begin(c, p) / KB) == tile) ? 0 : 1;
-                        const float* rp = p.ws + ((size_t)c * 2 + cs) * (size_t)(MP * NT);
+                        for (int m = 0; m < MP; ++m) __stcg(wp + m * NT + sb * 128 + n_local, v[sb][m]);
+                    // Every epilogue thread's stores precede the release.
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    if (et == 0) st_release_gpu(p.flags + blockIdx.x, p.epoch);
+                    do_out = false;
+                } else {
+                    float acc[NSUB][MP];
 #pragma unroll
-                        for (int sb = 0; sb < NSUB; ++sb)
+                    for (int sb = 0; sb < NSUB; ++sb)
 #pragma unroll
-                            for (int m = 0; m < MP; ++m) v[sb][m] += __ldcg(rp + m * NT + sb * 128 + n_local);
+                        for (int m = 0; m < MP; ++m) acc[sb][m] = 0.f;
+                    // The epilogue threads wait (bounded) for the other
+                    // contributors' flags in parallel, one each; the barrier
+                    // then orders every thread's loads after those acquires.
+                    bool mine = true;
+                    for (int i = et; i < c_last - c_first; i += 128)
+                        mine = mine && wait_flag(p.flags + c_first + i, p.epoch, abort_flag);
+                    const bool got = named_barrier_and<1, 128>(mine);
+                    if (got) {
+                        for (int c = c_first; c < c_last; ++c) {
+                            const float* rp = p.ws + (size_t)c * (size_t)(MP * NT);
+#pragma unroll
+                            for (int sb = 0; sb < NSUB; ++sb)
+#pragma unroll
+                                for (int m = 0; m < MP; ++m) acc[sb][m] += __ldcg(rp + m * NT + sb * 128 + n_local);
+                        }
                     }
+                    if (!got) break;
+#pragma unroll
+                    for (int sb = 0; sb < NSUB; ++sb)
+#pragma unroll
+                        for (int m = 0; m < MP; ++m) v[sb][m] = acc[sb][m] + v[sb][m];
+                    do_out = true;
                 }
             }
             if (do_out) {
@@ -608,15 +610,15 @@ int skinny_lockstep_slices(long long N, long long K, int sms) {
 }
 
 void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int* grid, size_t* ws_bytes,
-                     size_t* counter_bytes) {
+                     size_t* flag_bytes) {
     const long long tiles = (N + nt - 1) / nt;
     const long long work = tiles * ((K + 63) / 64);
     long long g = sms;
     if (g > work) g = work;
     if (g < 1) g = 1;
     *grid = (int)g;
-    *ws_bytes = (size_t)g * 2 * (size_t)skinny_mp(M) * (size_t)nt * sizeof(float);
-    *counter_bytes = (size_t)tiles * sizeof(unsigned long long);
+    *ws_bytes = (size_t)g * (size_t)skinny_mp(M) * (size_t)nt * sizeof(float);  // one slot per CTA
+    *flag_bytes = (size_t)g * sizeof(unsigned long long);
 }
 
 // Read on every call, like the other layout switches, so that a process
@@ -626,27 +628,25 @@ int skinny_env_nt() {
     return e ? atoi(e) : 0;
 }
 
-bool skinny_env_korder() {
-    const char* e = getenv("PAX_SKINNY_KORDER");
-    return e ? atoi(e) != 0 : false;
-}
 
 // Lockstep layout when there are no more column tiles than SMs; otherwise
 // persistent stream-K, one CTA per SM.  nt_force = 128 or 256 forces the
 // persistent layout with that unit width.
-SkinnyLayout skinny_layout(long long M, long long N, long long K, int sms, int nt_force, bool korder) {
+SkinnyLayout skinny_layout(long long M, long long N, long long K, int sms, int nt_force) {
     SkinnyLayout L;
     int nt = nt_force;
     L.slices = (nt == 0) ? skinny_lockstep_slices(N, K, sms) : 0;
     if (L.slices > 0) nt = 128;
     if (nt != 128 && nt != 256) nt = skinny_pick_nt(M, N, K, sms);
     L.nt = nt;
-    L.korder = L.slices == 0 && korder;
     skinny_geometry(M, N, K, sms, nt, &L.grid, &L.ws_bytes, &L.cnt_bytes);
     if (L.slices > 0) {
         const size_t per_cta = L.ws_bytes / (size_t)L.grid;
         L.grid = (int)(((N + 127) / 128) * L.slices);
         L.ws_bytes = per_cta * (size_t)L.grid;
+        L.cnt_bytes = (size_t)L.grid * sizeof(unsigned long long);
+        // One slice per tile splits nothing: no partial sums, no flags.
+        if (L.slices == 1) L.ws_bytes = L.cnt_bytes = 0;
     }
     return L;
 }
@@ -660,20 +660,20 @@ size_t skinny_smem_bytes(long long M, int nt) {
                     : mp == 48 ? SkCfg<48, 128>::SMEM_BYTES : SkCfg<64, 128>::SMEM_BYTES;
 }
 
-// Epoch of the next launch that uses arrival counters (never 0).
-static std::atomic<unsigned int> g_skinny_epoch{0};
-static unsigned int next_epoch() {
-    unsigned int e = ++g_skinny_epoch;
+// Epoch of the next launch (never 0).
+static std::atomic<unsigned long long> g_skinny_epoch{0};
+static unsigned long long next_epoch() {
+    unsigned long long e = ++g_skinny_epoch;
     while (e == 0) e = ++g_skinny_epoch;
     return e;
 }
-unsigned int skinny_last_epoch() { return g_skinny_epoch.load(); }
+unsigned long long skinny_last_epoch() { return g_skinny_epoch.load(); }
 
 int skinny_rotation_group();
 
 template <int MP, int NT>
-static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, bool korder, float* ws,
-                                       unsigned long long* counters, cudaStream_t stream) {
+static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, float* ws,
+                                       unsigned long long* flags, cudaStream_t stream) {
     using Cfg = SkCfg<MP, NT>;
     CUtensorMap tA, tB;
     const bool batched = pr.batch > 1;
@@ -691,13 +691,16 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
     p.work = (long long)p.num_tiles * p.kblocks;
     p.grid = grid;
     p.slices = slices;
-    p.korder = (slices == 0 && korder) ? 1 : 0;
+    // Stream-K visits each CTA's segments last to first: the head of its
+    // later tile, which it publishes, comes first, and the tail of its
+    // earlier tile, where it is the reducer, last.
+    p.korder = slices == 0 ? 1 : 0;
     // A rotation keeps each slice's k-blocks a whole lap only with one slice
     // per tile, outside batched launches.
     p.rot_group = (slices == 1 && !batched) ? skinny_rotation_group() : 0;
     p.b_early = (pr.b_const && pdl_enabled()) ? 1 : 0;
     p.ws = ws;
-    p.counters = counters;
+    p.flags = flags;
     p.epoch = next_epoch();
     p.c16 = pr.c_f16 ? static_cast<__half*>(pr.C) : nullptr;
     p.c32 = pr.c_f16 ? nullptr : static_cast<float*>(pr.C);
@@ -737,13 +740,13 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
 }
 
 template <int NT>
-static pax_status_t launch_skinny_nt(const Problem& p, int grid, int slices, bool korder, float* ws,
-                                     unsigned long long* counters, cudaStream_t stream) {
+static pax_status_t launch_skinny_nt(const Problem& p, int grid, int slices, float* ws,
+                                     unsigned long long* flags, cudaStream_t stream) {
     switch (skinny_mp(p.M)) {
-        case 16: return launch_skinny_impl<16, NT>(p, grid, slices, korder, ws, counters, stream);
-        case 32: return launch_skinny_impl<32, NT>(p, grid, slices, korder, ws, counters, stream);
-        case 48: return launch_skinny_impl<48, NT>(p, grid, slices, korder, ws, counters, stream);
-        default: return launch_skinny_impl<64, NT>(p, grid, slices, korder, ws, counters, stream);
+        case 16: return launch_skinny_impl<16, NT>(p, grid, slices, ws, flags, stream);
+        case 32: return launch_skinny_impl<32, NT>(p, grid, slices, ws, flags, stream);
+        case 48: return launch_skinny_impl<48, NT>(p, grid, slices, ws, flags, stream);
+        default: return launch_skinny_impl<64, NT>(p, grid, slices, ws, flags, stream);
     }
 }
 
@@ -759,14 +762,13 @@ int skinny_rotation_group() {
 }
 
 // nt: 128 or 256 output columns per unit.  slices > 0: lockstep layout (nt
-// 128, grid = tiles x slices); 0: persistent stream-K over `grid` CTAs,
-// segments in k order when korder is set.
-pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, unsigned long long* counters,
-                              cudaStream_t stream, int slices, bool korder) {
+// 128, grid = tiles x slices); 0: persistent stream-K over `grid` CTAs.
+pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, unsigned long long* flags,
+                              cudaStream_t stream, int slices) {
     if (p.M < 1 || p.M > kSkinnyMaxM || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL) return PAX_ERR_UNSUPPORTED;
-    if (slices > 0) return launch_skinny_nt<128>(p, grid, slices, false, ws, counters, stream);
-    if (nt == 256) return launch_skinny_nt<256>(p, grid, 0, korder, ws, counters, stream);
-    return launch_skinny_nt<128>(p, grid, 0, korder, ws, counters, stream);
+    if (slices > 0) return launch_skinny_nt<128>(p, grid, slices, ws, flags, stream);
+    if (nt == 256) return launch_skinny_nt<256>(p, grid, 0, ws, flags, stream);
+    return launch_skinny_nt<128>(p, grid, 0, ws, flags, stream);
 }
 
 // Self-test of the bounded waits (pax_selftest_bounded_wait): one thread
@@ -808,7 +810,7 @@ int read_clear_device_error_skinny() {
 // or a serving process that reserves the GPU's memory at start-up and treats
 // any later allocation as a failure), and latency-critical loops where the
 // implicit device synchronisation of cudaMalloc/cudaFree is not acceptable.
-// For them the skinny kernel's scratch (per-tile arrival counters followed
+// For them the skinny kernel's scratch (per-CTA publication flags followed
 // by the fp32 partial sums) lives in this fixed array instead of the
 // per-stream workspace.  Every GPU that loads the library holds it until the
 // process exits.
@@ -898,7 +900,7 @@ extern "C" pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cud
                              "pax_gemm_skinny_noalloc: needs 1 <= m <= 64, k >= 1 and 16-byte aligned rows");
     // The layout pax_gemm_ex would run (lockstep for up to one column tile
     // per SM, else stream-K), so that both entry points take the same time.
-    const SkinnyLayout L = skinny_layout(p.M, p.N, p.K, sms, skinny_env_nt(), skinny_env_korder());
+    const SkinnyLayout L = skinny_layout(p.M, p.N, p.K, sms, skinny_env_nt());
     const size_t cnt_pad = (L.cnt_bytes + 255) & ~size_t(255);
     if (cnt_pad + L.ws_bytes > kNoAllocScratchBytes) {
         char msg[160];
@@ -910,14 +912,12 @@ extern "C" pax_status_t pax_gemm_skinny_noalloc(const pax_gemm_desc_t* desc, cud
     void* scratch = nullptr;
     if (scratch_address(dev, &scratch) != PAX_OK)
         return report_status(PAX_ERR_CUDA, "pax_gemm_skinny_noalloc: cudaGetSymbolAddress failed");
-    // The array keeps whatever the previous call left; the counters must
-    // start at zero.  The lockstep layout with one K slice per tile splits no
-    // tile and uses no counters, so it needs no clear.
-    const bool uses_counters = !(L.slices == 1);
-    if (uses_counters && cudaMemsetAsync(scratch, 0, cnt_pad, stream) != cudaSuccess)
-        return report_status(PAX_ERR_CUDA, "pax_gemm_skinny_noalloc: counter reset failed");
+    // The array keeps whatever the previous call left.  Nothing in it has to
+    // start at zero: a publication flag counts only when it holds this
+    // launch's epoch (a 64-bit number no earlier launch in this process
+    // used), and a partial sum is read only after its flag.
     st = launch_skinny_ws(p, L.nt, L.grid, reinterpret_cast<float*>(static_cast<char*>(scratch) + cnt_pad),
-                          static_cast<unsigned long long*>(scratch), stream, L.slices, L.korder);
+                          static_cast<unsigned long long*>(scratch), stream, L.slices);
     if (st != PAX_OK) return report_status(st, "pax_gemm_skinny_noalloc: launch failed");
     return report_status(PAX_OK, "");
 }

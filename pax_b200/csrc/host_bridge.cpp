@@ -103,12 +103,11 @@ static Problem batch_item(const Problem& p, long long b) {
 // --------------------------------------------------------- workspaces
 // Split-K scratch of the skinny kernel, one buffer per stream so that
 // launches on different streams never share one.  Layout:
-// [per-tile arrival counters: cnt_cap bytes][partial sums: ws_cap bytes].
-// The counters are zero when the buffer is made; the kernel frees every
-// counter it used, and one that an aborted launch left behind carries an
-// older launch epoch, which later launches ignore.  The counter region never
-// moves or shrinks while the buffer lives.  Growing either region
-// reallocates and zeroes the whole buffer.
+// [per-CTA publication flags: cnt_cap bytes][partial sums: ws_cap bytes].
+// Nothing in it needs clearing between launches: a flag counts only when it
+// holds the current launch's epoch, and a flag that an earlier launch left
+// behind (finished, or aborted after a timed-out wait) holds an older one.
+// Growing either region reallocates the buffer.
 //
 // The key is (device, stream handle, thread).  The thread part is used only
 // for cudaStreamPerThread: that one handle value names a different stream in
@@ -137,7 +136,7 @@ static WsKey ws_key(int dev, cudaStream_t s) {
 }
 
 static pax_status_t get_workspace(int dev, cudaStream_t s, size_t cnt_need, size_t ws_need,
-                                  unsigned long long** counters, float** partials) {
+                                  unsigned long long** flags, float** partials) {
     std::lock_guard<std::mutex> lk(g_ws_mu);
     Workspace& w = g_ws[ws_key(dev, s)];
     if (w.cnt_cap < cnt_need || w.ws_cap < ws_need) {
@@ -161,20 +160,23 @@ static pax_status_t get_workspace(int dev, cudaStream_t s, size_t cnt_need, size
         w.cnt_cap = cnt_cap;
         w.ws_cap = ws_cap;
     }
-    *counters = static_cast<unsigned long long*>(w.ptr);
+    *flags = static_cast<unsigned long long*>(w.ptr);
     *partials = reinterpret_cast<float*>(static_cast<char*>(w.ptr) + w.cnt_cap);
     return PAX_OK;
 }
 
-// Test hook (pax_selftest_stale_counters): write into the arrival counters
-// of this stream's workspace what a launch that gave up on a timed-out wait
-// leaves behind, one arrival under the latest launch epoch.
+// Test hook (pax_selftest_stale_counters): write into the publication
+// flags of this stream's workspace what launches that gave up on a
+// timed-out wait leave behind: flags holding the latest launch epoch, and
+// older ones.
 static pax_status_t poison_workspace_counters(int dev, cudaStream_t s) {
     std::lock_guard<std::mutex> lk(g_ws_mu);
     auto it = g_ws.find(ws_key(dev, s));
     if (it == g_ws.end() || !it->second.ptr) return PAX_ERR_INVALID;
     const size_t n = it->second.cnt_cap / sizeof(unsigned long long);
-    std::vector<unsigned long long> v(n, ((unsigned long long)skinny_last_epoch() << 32) | 1ull);
+    std::vector<unsigned long long> v(n);
+    const unsigned long long last = skinny_last_epoch();
+    for (size_t i = 0; i < n; ++i) v[i] = (i % 2 == 0 || last < 2) ? last : last - 1;
     if (cudaStreamSynchronize(s) != cudaSuccess ||
         cudaMemcpy(it->second.ptr, v.data(), n * sizeof(unsigned long long), cudaMemcpyHostToDevice) != cudaSuccess)
         return PAX_ERR_CUDA;
@@ -315,8 +317,7 @@ static size_t kernel_smem_bytes(const Problem& p, pax_algo_t algo, int sms) {
     if (algo == PAX_ALGO_TC || algo == PAX_ALGO_TC2) return tc_smem_bytes(shape, p.c_f16);
     if (algo == PAX_ALGO_SKINNY && p.M <= kSkinnyMaxM)
         return skinny_smem_bytes(p.M, p.batch > 1 ? 128
-                                                  : skinny_layout(p.M, p.N, p.K, sms, skinny_env_nt(),
-                                                                  skinny_env_korder()).nt);
+                                                  : skinny_layout(p.M, p.N, p.K, sms, skinny_env_nt()).nt);
     return 0;
 }
 
@@ -340,7 +341,7 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
             return fail(PAX_ERR_UNSUPPORTED, "skinny path needs m <= %lld and 16-byte aligned rows", kSkinnyMaxM);
         const long long units = p.batch * ((p.N + 127) / 128);
         const int grid = (int)(units < di.sms ? units : di.sms);
-        st = launch_skinny_ws(p, 128, grid, nullptr, nullptr, s, 0, false);
+        st = launch_skinny_ws(p, 128, grid, nullptr, nullptr, s, 0);
         if (st != PAX_OK) return fail(st, "launch failed: %s", cudaGetErrorString(cudaGetLastError()));
         return set_status(PAX_OK);
     }
@@ -367,16 +368,15 @@ static pax_status_t run(const Problem& p, pax_algo_t algo, cudaStream_t s) {
                             kSkinnyMaxM);
             // Lockstep layout when there are no more column tiles than SMs;
             // otherwise persistent stream-K, one CTA per SM.
-            // PAX_SKINNY_NT=128|256 forces the persistent layout;
-            // PAX_SKINNY_KORDER=1 visits its segments in k order.
-            const SkinnyLayout L = skinny_layout(p.M, p.N, p.K, di.sms, skinny_env_nt(), skinny_env_korder());
+            // PAX_SKINNY_NT=128|256 forces the persistent layout.
+            const SkinnyLayout L = skinny_layout(p.M, p.N, p.K, di.sms, skinny_env_nt());
             const size_t cnt_pad = (L.cnt_bytes + 255) & ~size_t(255);
-            unsigned long long* counters = nullptr;
+            unsigned long long* flags = nullptr;
             float* partials = nullptr;
-            st = get_workspace(dev, s, cnt_pad, L.ws_bytes, &counters, &partials);
+            st = get_workspace(dev, s, cnt_pad, L.ws_bytes, &flags, &partials);
             if (st != PAX_OK)
                 return fail(st, "skinny workspace allocation failed (%zu bytes)", cnt_pad + L.ws_bytes);
-            st = launch_skinny_ws(p, L.nt, L.grid, partials, counters, s, L.slices, L.korder);
+            st = launch_skinny_ws(p, L.nt, L.grid, partials, flags, s, L.slices);
             break;
         }
         case PAX_ALGO_SIMT: st = launch_simt(p, s); break;
@@ -622,7 +622,7 @@ int pax_gemm_pipeline_stages(const pax_gemm_desc_t* desc) {
     choose_kernel(p, sms, &a, &shape);
     if (a == PAX_ALGO_TC || a == PAX_ALGO_TC2) return tc_stages(shape);
     if (a == PAX_ALGO_SKINNY)
-        return skinny_stages(p.M, skinny_layout(p.M, p.N, p.K, sms, skinny_env_nt(), skinny_env_korder()).nt);
+        return skinny_stages(p.M, skinny_layout(p.M, p.N, p.K, sms, skinny_env_nt()).nt);
     return 0;  // CUDA-core kernel: no TMA ring
 }
 

@@ -59,36 +59,34 @@ struct TcPlan {
 TcPlan tc_plan(const Problem& p, int shape, int dev, int sms, bool allow_halves, cudaStream_t stream);
 pax_status_t launch_tc(const Problem& p, const TcPlan& plan, cudaStream_t stream);
 pax_status_t launch_simt(const Problem& p, cudaStream_t stream);
-// Skinny kernel, nt (128 or 256) output columns per work unit: `ws` holds
-// grid*2*MP*nt fp32 partial sums and `counters` one 64-bit arrival counter
-// per nt-column tile.  Counters are zero when first used; the kernel frees
-// each one it used, and a counter an aborted launch left behind carries an
-// older launch epoch, which the next launch ignores.  skinny_geometry gives
-// the grid and both sizes; skinny_pick_nt the unit width.
+// Skinny kernel, nt (128 or 256) output columns per work unit.  A tile split
+// between CTAs is summed by its last contributor: the others each put their
+// partial sum in their slot of `ws` (MP*nt fp32 per CTA) and set their entry
+// of `flags` (one word per CTA) to the launch's epoch.  Nothing needs
+// clearing between launches: a flag from an earlier launch, finished or
+// aborted, holds an older epoch.  skinny_geometry gives the grid and both
+// sizes; skinny_pick_nt the unit width.
 int skinny_pick_nt(long long M, long long N, long long K, int sms);
 int skinny_lockstep_slices(long long N, long long K, int sms);
 void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int* grid, size_t* ws_bytes,
-                     size_t* counter_bytes);
+                     size_t* flag_bytes);
 // The layout pax_gemm_ex runs for a skinny problem: nt, grid, K slices
-// (lockstep layout when > 0), k-ordered stream-K, and the workspace sizes.
+// (lockstep layout when > 0), and the workspace sizes.
 struct SkinnyLayout {
     int nt = 128, grid = 1, slices = 0;
-    bool korder = false;
-    size_t ws_bytes = 0, cnt_bytes = 0;
+    size_t ws_bytes = 0, cnt_bytes = 0;  // partial sums, flags
 };
 // nt_force = 128 or 256 forces persistent stream-K with that unit width
-// (PAX_SKINNY_NT); korder visits its segments in k order (PAX_SKINNY_KORDER).
-SkinnyLayout skinny_layout(long long M, long long N, long long K, int sms, int nt_force, bool korder);
+// (PAX_SKINNY_NT).
+SkinnyLayout skinny_layout(long long M, long long N, long long K, int sms, int nt_force);
 int skinny_env_nt();
-bool skinny_env_korder();
-// Epoch of the most recent launch that was given arrival counters.
-unsigned int skinny_last_epoch();
+// Epoch of the most recent launch of the skinny kernel.
+unsigned long long skinny_last_epoch();
 // slices > 0 = the lockstep layout (nt 128, `grid` = tiles x slices CTAs,
-// one per SM); its workspace is sized by skinny_geometry with that grid's
-// per-CTA share.  slices = 0: persistent stream-K, each CTA's segments in
-// k order (its later tile's head first) when korder is set.
-pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, unsigned long long* counters,
-                              cudaStream_t stream, int slices = 0, bool korder = false);
+// one per SM); 0: persistent stream-K, `grid` CTAs, each CTA's segments
+// last to first (the head of its later tile first).
+pax_status_t launch_skinny_ws(const Problem& p, int nt, int grid, float* ws, unsigned long long* flags,
+                              cudaStream_t stream, int slices = 0);
 // Forget the cached device address of the allocation-free path's scratch
 // array (pax_shutdown).
 void skinny_forget_scratch();

@@ -120,6 +120,39 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     return mbar_wait_slow<kCluster>(bar, parity, abort_flag);
 }
 
+// ------------------------------------------------- flags between CTAs
+__device__ __forceinline__ void st_release_gpu(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Slow path of wait_flag: poll with the limit of abandonable waits.
+static __device__ __noinline__ bool wait_flag_slow(const unsigned long long* flag, unsigned long long value,
+                                            volatile int* abort_flag) {
+    const unsigned long long t0 = globaltimer_ns();
+    const unsigned long long limit = g_pax_wait_limit_ns;
+    for (;;) {
+        __nanosleep(64);
+        if (ld_acquire_gpu(flag) == value) return true;
+        if (abort_flag != nullptr && *abort_flag) return false;
+        if (globaltimer_ns() - t0 > limit) {
+            if (abort_flag != nullptr) *abort_flag = 1;
+            atomicOr(&g_pax_device_error, PAX_DEVERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+// Bounded wait, with acquire semantics, until another CTA of the grid has
+// release-stored `value` to *flag.  False on timeout or abort.
+__device__ __forceinline__ bool wait_flag(const unsigned long long* flag, unsigned long long value,
+                                          volatile int* abort_flag) {
+    if (ld_acquire_gpu(flag) == value) return true;
+    return wait_flag_slow(flag, value, abort_flag);
+}
+
 // --------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -411,12 +444,32 @@ __device__ __forceinline__ uint4 ld_nc_v4_hint(const void* p, uint64_t pol) {
                  : "l"(p), "l"(pol));
     return r;
 }
+__device__ __forceinline__ uint4 ld_nc_v4_l1_hint(const void* p, uint64_t pol) {
+    uint4 r;
+    asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p), "l"(pol));
+    return r;
+}
+__device__ __forceinline__ uint4 ld_nc_v4_l1(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
     uint4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p));
     return r;
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+    uint4 r;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr) : "memory");
+    return r;
+}
+__device__ __forceinline__ void st_global_v4(void* p, const uint4& u) {
+    asm volatile("st.global.v4.b32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(u.x), "r"(u.y), "r"(u.z), "r"(u.w) : "memory");
 }
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)

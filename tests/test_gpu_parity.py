@@ -113,16 +113,15 @@ def test_skinny(cuda, rng, M, NK):
     check(got, oracle.gemm(A, B, epi="bias", bias=bias, out_dtype=np.float16), np.float16)
 
 
-@pytest.mark.parametrize("nt,korder", [(0, 0), (128, 0), (256, 0), (128, 1), (256, 1)])
+@pytest.mark.parametrize("nt", [0, 128, 256])
 @pytest.mark.parametrize("M,N,K", [(16, 16384, 4096), (1, 1000, 320), (33, 2048, 1088), (64, 768, 4096),
-                                   (16, 520, 64), (16, 40960, 2048), (48, 16384, 4160)])
-def test_skinny_layouts(cuda, rng, monkeypatch, nt, korder, M, N, K):
+                                   (16, 520, 64), (16, 40960, 2048), (48, 16384, 4160), (16, 128, 4096)])
+def test_skinny_layouts(cuda, rng, monkeypatch, nt, M, N, K):
     """Lockstep layout (nt=0: one CTA per (tile, interleaved K slice)) and the
-    persistent stream-K layout with 128- and 256-column units, segments
-    first-to-last or in k order (korder), including ragged N, uneven K
-    slices and tiles split between CTAs."""
+    persistent stream-K layout with 128- and 256-column units, including
+    ragged N, uneven K slices, tiles split between two or three CTAs and a
+    single tile split over every SM."""
     monkeypatch.setenv("PAX_SKINNY_NT", str(nt))
-    monkeypatch.setenv("PAX_SKINNY_KORDER", str(korder))
     A, B = inputs(rng, M, N, K, dist="normal")
     bias = rng.standard_normal(N).astype(np.float16)
     got = run_gemm(A, B, cuda, epi="bias", bias=bias, out_dtype=np.float16, algo="skinny")
@@ -140,14 +139,14 @@ def test_skinny_epilogues(cuda, rng, epi, out):
     check(got, oracle.gemm(A, B, epi=epi, bias=bias, residual=res, out_dtype=out), out)
 
 
-@pytest.mark.parametrize("korder", [0, 1])
-def test_skinny_stream_k_bit_exact_and_deterministic(cuda, rng, monkeypatch, korder):
-    """Integer-valued inputs through stream-K with split tiles: exact, and
-    the same bits on every run (partials are summed in CTA order)."""
-    monkeypatch.setenv("PAX_SKINNY_NT", "128")
-    monkeypatch.setenv("PAX_SKINNY_KORDER", str(korder))
+@pytest.mark.parametrize("nt", ["128", "0"])
+def test_skinny_stream_k_bit_exact_and_deterministic(cuda, rng, monkeypatch, nt):
+    """Integer-valued inputs through split tiles (stream-K; lockstep with K
+    slices at N = 4096): exact, and the same bits on every run (a tile's
+    last contributor adds the others' partial sums in CTA order)."""
+    monkeypatch.setenv("PAX_SKINNY_NT", nt)
     A = rng.integers(-3, 4, (16, 4096)).astype(np.float16)
-    B = rng.integers(-3, 4, (4096, 16384)).astype(np.float16)
+    B = rng.integers(-3, 4, (4096, 16384 if nt == "128" else 4096)).astype(np.float16)
     exact = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.float32)
     first = run_gemm(A, B, cuda, out_dtype=np.float32, algo="skinny")
     assert np.array_equal(first, exact)
