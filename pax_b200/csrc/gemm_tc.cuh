@@ -50,12 +50,6 @@ struct TcParams {
     int tiles_m, tiles_n, num_tiles;
     int group_m;  // output tiles are visited in column-major groups of group_m tile rows
     int c_evict_first;  // store C with an L2 evict-first policy (C much larger than L2)
-    int res_mode;       // residual loads: 0 L1 no-allocate, 1 + L2 evict-first, 2 L1 + L2 evict-first, 3 L1
-    // Output stores: 0 = TMA tile stores from the staging buffer; 1 = the
-    // staging buffer read back in row order and written with 16-byte stores.
-    int lsu_store;
-    void* c;            // C (item 0), row pitch ldc elements, items sc elements apart
-    long long ldc, sc;
     // Work items: tiles [0, full_items) whole, then the last tail_tiles tiles
     // (the tail wave) as two column halves each, so
     // num_items = full_items + 2 * tail_tiles.
@@ -81,7 +75,6 @@ struct TcParams {
 constexpr int kTcMaxReplicas = 7;
 struct TcReplicas {
     CUtensorMap map[kTcMaxReplicas];
-    void* ptr[kTcMaxReplicas];  // the same buffers, for the store path without TMA
     int n;
 };
 
@@ -436,7 +429,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         const int q = warp & 3;          // TMEM lane quarter this warp may read
         const int wh = (warp - 2) >> 2;  // which half of the item's columns
         uint8_t* sbuf = sStg + (warp - 2) * Cfg::STG_BYTES;
-        // Residual and (when much larger than L2) C pass through L2 once.
+        // C much larger than L2 passes through it once.
         const uint64_t pol_stream = l2_evict_first_policy();
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -458,7 +451,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             // waiting for it: this warp's bias and the first residual chunk.
             const uint4 bias8 = bias_tile_load(tcol0, wcols, lane, p.N, ep);
             ResChunk<32, RES> rc;
-            if (wcols > 0) res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, ep, pol_stream, p.res_mode);
+            if (wcols > 0) res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, ep);
             bool ok = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
@@ -501,7 +494,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     // sub-chunk's loads, which then overlap the GeLU math below.
                     if constexpr (RES != 0) {
                         if (c + 32 < nch * EC)
-                            res_prefetch<32, RES>(rc, row, tcol0 + c + 32, p.M, p.N, ep, pol_stream, p.res_mode);
+                            res_prefetch<32, RES>(rc, row, tcol0 + c + 32, p.M, p.N, ep);
                     }
                     epi_gelu<32, GELU>(v);
 #pragma unroll
@@ -514,7 +507,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                 }
                 // The staging buffer is free once this warp's previous store
                 // has finished reading it.
-                if (lane == 0 && !p.lsu_store) bulk_wait_read<0>();
+                if (lane == 0) bulk_wait_read<0>();
                 __syncwarp();
                 const uint32_t srow = smem_u32(sbuf) + (uint32_t)lane * 128u;
 #pragma unroll
@@ -522,39 +515,6 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     // 128B swizzle: 16-byte chunk j of row r lives at chunk j ^ (r % 8).
                     st_shared_v4(srow + (uint32_t)((j ^ (lane & 7)) << 4), w[4 * j], w[4 * j + 1], w[4 * j + 2],
                                  w[4 * j + 3]);
-                }
-                if (p.lsu_store) {
-                    // Read the 32 x 128 B chunk back row by row: each load and
-                    // store instruction covers four whole 128-byte rows.
-                    __syncwarp();
-                    constexpr int PIECE = 16 / (int)sizeof(OutT);  // elements per 16 B
-                    const int j = lane & 7;
-                    const long long col = tcol0 + ci * EC + j * PIECE;
-                    char* cbase = static_cast<char*>(p.c) + (long long)bz * p.sc * (long long)sizeof(OutT);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int r = 4 * i + (lane >> 3);
-                        const uint4 u = ld_shared_v4(smem_u32(sbuf) + (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)));
-                        const long long grow = (long long)row0 + r;
-                        if (grow >= p.M || col >= p.N) continue;
-                        const long long off = (grow * p.ldc + col) * (long long)sizeof(OutT);
-                        if (col + PIECE <= p.N) {
-                            st_global_v4(cbase + off, u);
-                            for (int d = 0; d < reps.n; ++d)
-                                st_global_v4(static_cast<char*>(reps.ptr[d]) + (long long)bz * p.sc * (long long)sizeof(OutT) + off, u);
-                        } else {
-                            // Ragged right edge: element by element.
-                            const OutT* e = reinterpret_cast<const OutT*>(&u);
-                            for (int x = 0; x < PIECE && col + x < p.N; ++x) {
-                                reinterpret_cast<OutT*>(cbase + off)[x] = e[x];
-                                for (int d = 0; d < reps.n; ++d)
-                                    reinterpret_cast<OutT*>(static_cast<char*>(reps.ptr[d]) +
-                                                            (long long)bz * p.sc * (long long)sizeof(OutT) + off)[x] = e[x];
-                            }
-                        }
-                    }
-                    __syncwarp();  // the staging buffer is read before it is rewritten
-                    continue;
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -573,10 +533,12 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                 acc_phase ^= 1u;
             }
         }
-        if (lane == 0) bulk_wait<0>();
-        // Stores to other GPUs are complete; make them visible system-wide
-        // before the grid ends.
-        if (reps.n > 0 && (p.lsu_store || lane == 0)) __threadfence_system();
+        if (lane == 0) {
+            bulk_wait<0>();
+            // Stores to other GPUs are complete; make them visible system-wide
+            // before the grid ends.
+            if (reps.n > 0) __threadfence_system();
+        }
         __syncwarp();
     }
 
@@ -661,7 +623,6 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     memset(&reps, 0, sizeof(reps));
     if (pr.n_replicas < 0 || pr.n_replicas > kTcMaxReplicas) return PAX_ERR_INVALID;
     reps.n = pr.n_replicas;
-    for (int d = 0; d < reps.n; ++d) reps.ptr[d] = pr.replicas[d];
     for (int d = 0; d < reps.n; ++d)
         if (!make_tmap(&reps.map[d], pr.replicas[d], f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                        pr.N, pr.M, pr.batch, pr.ldc * ce, zstride(pr.batch > 1 ? pr.sc : 0, pr.M, pr.ldc * ce, ce),
@@ -700,13 +661,6 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     const long long c_bytes = pr.M * pr.N * (long long)ce * pr.batch;
     p.c_evict_first = c_bytes > (64LL << 20) ? 1 : 0;
     if (const char* e = getenv("PAX_TC_C_EVICT")) p.c_evict_first = atoi(e) != 0 ? 1 : 0;
-    p.res_mode = 3;
-    if (const char* e = getenv("PAX_TC_RES_MODE")) p.res_mode = atoi(e) & 3;
-    p.lsu_store = 0;
-    if (const char* e = getenv("PAX_TC_LSU")) p.lsu_store = atoi(e) != 0 ? 1 : 0;
-    p.c = pr.C;
-    p.ldc = pr.ldc;
-    p.sc = pr.batch > 1 ? pr.sc : 0;
     p.full_items = plan.full_items;
     p.tail_tiles = plan.tail_tiles;
     p.num_items = plan.full_items + 2 * plan.tail_tiles;

@@ -429,47 +429,18 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, bool a_mn_ma
 }
 
 // ----------------------------------------------------------- misc memory
-// L2 policy that marks lines as first to evict: for data read or written
-// once (a residual, an output much larger than L2), so that it does not push
-// the reused operand tiles out of L2.
+// L2 policy that marks lines as first to evict: for data written once and
+// much larger than L2 (an output), so that it does not push the reused
+// operand tiles out of L2.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
     return pol;
 }
-__device__ __forceinline__ uint4 ld_nc_v4_hint(const void* p, uint64_t pol) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p), "l"(pol));
-    return r;
-}
-__device__ __forceinline__ uint4 ld_nc_v4_l1_hint(const void* p, uint64_t pol) {
-    uint4 r;
-    asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p), "l"(pol));
-    return r;
-}
 __device__ __forceinline__ uint4 ld_nc_v4_l1(const void* p) {
     uint4 r;
     asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
     return r;
-}
-__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
-}
-__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
-    uint4 r;
-    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr) : "memory");
-    return r;
-}
-__device__ __forceinline__ void st_global_v4(void* p, const uint4& u) {
-    asm volatile("st.global.v4.b32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(u.x), "r"(u.y), "r"(u.z), "r"(u.w) : "memory");
 }
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
