@@ -841,30 +841,53 @@ def run_pax(args):
     # replicated (fused and NCCL), and C5 split over the ranks.
     sub = {}
     defaults = args.config == 2 and not args.epilogue and args.m is None and not args.strong and not args.gather
+
+    def guarded(name, fn):
+        """Run one sub-record; an error is recorded in the line instead of
+        losing the headline.  Every rank takes the same steps, and the ranks
+        agree (one all-reduce) on whether all of them succeeded, so that none
+        goes on into later collectives alone."""
+        try:
+            out, ok = fn(), 1
+        except Exception as e:  # noqa: BLE001 - reported in the JSON line
+            out, ok = {"error": f"{type(e).__name__}: {e}"[:300]}, 0
+        if world > 1:
+            t = torch.tensor([ok], dtype=torch.int32, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            ok = int(t.item())
+        torch.cuda.empty_cache()
+        return out, ok == 1
+
     if defaults and not args.no_subrecords:
+        ok = True
         if world == 1:
             sub["configs"] = {}
             for cid, st, wu in ((1, args.steps, max(3, args.warmup)), (3, min(args.steps, 20), max(3, args.warmup)),
                                 (4, args.steps, max(3, args.warmup))):
-                sub["configs"][f"C{cid}"] = config_record(cid, args, dev, flush, peak, hbm, st, wu)
+                sub["configs"][f"C{cid}"], _ = guarded(
+                    f"C{cid}", lambda cid=cid, st=st, wu=wu: config_record(cid, args, dev, flush, peak, hbm, st, wu))
         else:
-            sub["gather"] = gather_record(A, B, bias, res, cfg, M, N, n_total, dev, flush, world, local,
-                                          min(args.steps, 20), max(3, args.warmup))
-        # C5 over the ranks: 55 ms per launch on one GPU, so a few steps.
-        c5 = split_record(args, dev, flush, peak, world, rank, local, 3, 3, gather_too=True)
-        if world == 1:
-            a = c5["tflops_total"]
-            c5["roofline"] = {"bound": "tensor", "achieved": a, "peak": peak, "unit": "TFLOP/s", "frac": a / peak,
-                              "traffic": traffic_from_profiles(5)}
-            c5["lean_pipeline_bound"] = lean_bound(a / peak, c5["kernel"]["stages"])
-            sub["configs"]["C5"] = c5
-        else:
-            sub["c5_split"] = c5
+            sub["gather"], ok = guarded("gather", lambda: gather_record(
+                A, B, bias, res, cfg, M, N, n_total, dev, flush, world, local, min(args.steps, 20),
+                max(3, args.warmup)))
+        if ok:
+            # C5 over the ranks: 55 ms per launch on one GPU, so a few steps.
+            c5, _ = guarded("c5", lambda: split_record(args, dev, flush, peak, world, rank, local, 3, 3,
+                                                       gather_too=True))
+            if world == 1:
+                if "tflops_total" in c5:
+                    a = c5["tflops_total"]
+                    c5["roofline"] = {"bound": "tensor", "achieved": a, "peak": peak, "unit": "TFLOP/s",
+                                      "frac": a / peak, "traffic": traffic_from_profiles(5)}
+                    c5["lean_pipeline_bound"] = lean_bound(a / peak, c5["kernel"]["stages"])
+                sub["configs"]["C5"] = c5
+            else:
+                sub["c5_split"] = c5
 
     # Clocks over a long back-to-back run of the headline step: enough NVML
     # samples to say what SM clock the kernel runs at under sustained load.
     if defaults and world == 1 and not args.no_subrecords:
-        sub["sustained"] = sustained_record(step, dev, local, flops_rank)
+        sub["sustained"], _ = guarded("sustained", lambda: sustained_record(step, dev, local, flops_rank))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -65,13 +65,19 @@ struct SkinnyParams {
 
 // MP: M padded to a multiple of 16 (the MMA N).  NT: output columns per work
 // unit, NT/128 MMAs of M = 128 per k-step.  Wider units make each k-row of B
-// a longer contiguous DRAM burst (NT * 2 bytes).
-template <int MP_, int NT_>
+// a longer contiguous DRAM burst (NT * 2 bytes).  BK: k-rows per ring slot
+// (a "k-block"), 64 or 128.  With 128 every slot holds two 64-wide k-steps'
+// worth: half the TMA instructions, barrier operations and MMA commits per
+// byte of B (on C4 the MMA issue and release of a slot cost about 12 % of
+// the streaming rate with 64).
+template <int MP_, int NT_, int BK_>
 struct SkCfg {
-    static constexpr int MP = MP_, NT = NT_, BK = 64;
+    static constexpr int MP = MP_, NT = NT_, BK = BK_;
     static constexpr int NSUB = NT / 128;
-    static constexpr uint32_t B_BYTES = NT * BK * 2;   // NT/64 boxes of 64n x 64k
-    static constexpr uint32_t A_BYTES = MP * BK * 2;   // MP rows of 128 bytes
+    static constexpr uint32_t B_COL_BYTES = BK * 128;  // one 64-column box: BK rows of 128 bytes
+    static constexpr uint32_t B_BYTES = NT * BK * 2;   // NT/64 boxes of 64n x BK k
+    static constexpr uint32_t A_HALF_BYTES = MP * 128; // MP rows of 64 k (128 bytes)
+    static constexpr uint32_t A_BYTES = MP * BK * 2;   // BK/64 such boxes
     static constexpr uint32_t STAGE_BYTES = B_BYTES + A_BYTES;
     static constexpr int STAGES = (225 * 1024) / STAGE_BYTES;
     static constexpr uint32_t ACC_COLS = NSUB * MP;  // one accumulator: NSUB blocks of MP columns
@@ -83,7 +89,8 @@ struct SkCfg {
     static constexpr uint32_t IDESC = umma_idesc_f16(128, MP, /*a_mn*/ true, /*b_mn*/ false);
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
     static_assert(STAGES >= 3, "at least three stages in flight");
-    static_assert(A_BYTES % 1024 == 0, "A slot must keep 1024-byte swizzle alignment");
+    static_assert(A_HALF_BYTES % 1024 == 0, "A boxes must keep 1024-byte swizzle alignment");
+    static_assert(BK == 64 || BK == 128, "k-block of 64 or 128");
     static_assert(2 * ACC_COLS <= 512, "two accumulators must fit in TMEM");
 };
 
@@ -187,11 +194,11 @@ __device__ __forceinline__ int sk_kblock(const SkinnyParams& p, const SkSeg& sg,
     return kb;
 }
 
-template <int MP, int NT>
+template <int MP, int NT, int BK>
 __global__ void __launch_bounds__(192, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const SkinnyParams p) {
-    using Cfg = SkCfg<MP, NT>;
+    using Cfg = SkCfg<MP, NT, BK>;
     constexpr int STAGES = Cfg::STAGES;
     constexpr int NSUB = Cfg::NSUB;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -263,7 +270,7 @@ __global__ void __launch_bounds__(192, 1)
                 const uint32_t bdst = smem_u32(sB + jj * Cfg::B_BYTES);
 #pragma unroll
                 for (int b = 0; b < NT / 64; ++b)
-                    tma_load_3d(bdst + b * 8192u, &tmB, fb, tl0 * NT + b * 64, kb * 64, zb0);
+                    tma_load_3d(bdst + b * Cfg::B_COL_BYTES, &tmB, fb, tl0 * NT + b * 64, kb * BK, zb0);
             }
         }
         pdl_wait();  // A and B may be written by the previous grid
@@ -279,9 +286,12 @@ __global__ void __launch_bounds__(192, 1)
                 // bytes of every k-row of B.
 #pragma unroll
                 for (int b = 0; b < NT / 64; ++b)
-                    tma_load_3d(bdst + b * 8192u, &tmB, fb, tl0 * NT + b * 64, kb * 64, zb0);
+                    tma_load_3d(bdst + b * Cfg::B_COL_BYTES, &tmB, fb, tl0 * NT + b * 64, kb * BK, zb0);
             }
-            tma_load_3d(smem_u32(sA + jj * Cfg::A_BYTES), &tmA, fb, kb * 64, 0, za0);
+#pragma unroll
+            for (int h = 0; h < BK / 64; ++h)
+                tma_load_3d(smem_u32(sA + jj * Cfg::A_BYTES + h * Cfg::A_HALF_BYTES), &tmA, fb, kb * BK + h * 64, 0,
+                            za0);
         }
         p_issued = (1u << nfill) - 1u;  // all at phase 0
         p_j = nfill;
@@ -320,8 +330,11 @@ __global__ void __launch_bounds__(192, 1)
                     const uint32_t bdst = smem_u32(sB + p_stage * Cfg::B_BYTES);
 #pragma unroll
                     for (int b = 0; b < NT / 64; ++b)
-                        tma_load_3d(bdst + b * 8192u, &tmB, fb, tile * NT + b * 64, kb * 64, zb);
-                    tma_load_3d(smem_u32(sA + p_stage * Cfg::A_BYTES), &tmA, fb, kb * 64, 0, za);
+                        tma_load_3d(bdst + b * Cfg::B_COL_BYTES, &tmB, fb, tile * NT + b * 64, kb * BK, zb);
+#pragma unroll
+                    for (int h = 0; h < BK / 64; ++h)
+                        tma_load_3d(smem_u32(sA + p_stage * Cfg::A_BYTES + h * Cfg::A_HALF_BYTES), &tmA, fb,
+                                    kb * BK + h * 64, 0, za);
                     p_issued |= 1u << p_stage;
                     p_last_parity = (p_last_parity & ~(1u << p_stage)) | (p_phase << p_stage);
                     if (++p_stage == STAGES) {
@@ -346,7 +359,7 @@ __global__ void __launch_bounds__(192, 1)
             bool ok = true;
             long long cur = sk_cursor0(p);
             SkSeg sg;
-            const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB), 8192, 1024);  // B^T, N-major
+            const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB), Cfg::B_COL_BYTES, 1024);  // B^T, N-major
             const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA), 16, 1024);    // A, K-major
             while (ok && sk_next_seg(p, cur, sg)) {
                 if (!mbar_wait(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag)) break;
@@ -361,11 +374,16 @@ __global__ void __launch_bounds__(192, 1)
                     const uint64_t bs = bdesc0 + (uint64_t)((stage * Cfg::B_BYTES) >> 4);
                     const uint64_t as = adesc0 + (uint64_t)((stage * Cfg::A_BYTES) >> 4);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
+                    for (int kk = 0; kk < BK / 16; ++kk) {
 #pragma unroll
                         for (int sb = 0; sb < NSUB; ++sb) {
-                            const uint64_t ad = bs + (uint64_t)((sb * 16384 + kk * 2048) >> 4);
-                            const uint64_t bd = as + (uint64_t)((kk * 32) >> 4);
+                            // B^T: sub-tile sb is column boxes 2sb, 2sb+1; k-step
+                            // kk is 16 k-rows further in.  A: 64-k box kk/4,
+                            // 32 bytes further per k-step within it.
+                            const uint64_t ad =
+                                bs + (uint64_t)((sb * 2 * Cfg::B_COL_BYTES + kk * 2048) >> 4);
+                            const uint64_t bd =
+                                as + (uint64_t)(((kk / 4) * Cfg::A_HALF_BYTES + (kk % 4) * 32) >> 4);
                             tc_mma_f16(d_tmem + (uint32_t)(sb * MP), ad, bd, Cfg::IDESC,
                                        (v != 0 || kk != 0) ? 1u : 0u);
                         }
@@ -576,13 +594,17 @@ static bool sk_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
 
 int skinny_mp(long long M) { return (int)((M + 15) / 16) * 16; }
 
+// k-rows per ring slot: 128 for 128-column units with m <= 32 (five or six
+// slots of 36-40 KB), else 64 (the wider slots would leave too few).
+int skinny_bk(long long M, int nt) { return (nt == 128 && skinny_mp(M) <= 32) ? 128 : 64; }
+
 int skinny_stages(long long M, int nt) {
     const int mp = skinny_mp(M);
     if (nt == 256)
-        return mp == 16 ? SkCfg<16, 256>::STAGES : mp == 32 ? SkCfg<32, 256>::STAGES
-                         : mp == 48 ? SkCfg<48, 256>::STAGES : SkCfg<64, 256>::STAGES;
-    return mp == 16 ? SkCfg<16, 128>::STAGES : mp == 32 ? SkCfg<32, 128>::STAGES
-                     : mp == 48 ? SkCfg<48, 128>::STAGES : SkCfg<64, 128>::STAGES;
+        return mp == 16 ? SkCfg<16, 256, 64>::STAGES : mp == 32 ? SkCfg<32, 256, 64>::STAGES
+                         : mp == 48 ? SkCfg<48, 256, 64>::STAGES : SkCfg<64, 256, 64>::STAGES;
+    return mp == 16 ? SkCfg<16, 128, 128>::STAGES : mp == 32 ? SkCfg<32, 128, 128>::STAGES
+                     : mp == 48 ? SkCfg<48, 128, 64>::STAGES : SkCfg<64, 128, 64>::STAGES;
 }
 
 int skinny_pick_nt(long long M, long long N, long long K, int sms) {
@@ -600,9 +622,10 @@ int skinny_pick_nt(long long M, long long N, long long K, int sms) {
 // split only when there are SMs to spare for it.  Returns the number of K
 // slices (floor(SMs / tiles), at least 1), or 0 when there are more tiles
 // than SMs (persistent stream-K balances those better).
-int skinny_lockstep_slices(long long N, long long K, int sms) {
+int skinny_lockstep_slices(long long M, long long N, long long K, int sms) {
     const long long tiles = (N + 127) / 128;
-    const long long kb = (K + 63) / 64;
+    const long long bk = skinny_bk(M, 128);
+    const long long kb = (K + bk - 1) / bk;
     if (tiles > sms) return 0;
     long long s = sms / tiles;
     if (s > kb) s = kb;
@@ -612,7 +635,8 @@ int skinny_lockstep_slices(long long N, long long K, int sms) {
 void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int* grid, size_t* ws_bytes,
                      size_t* flag_bytes) {
     const long long tiles = (N + nt - 1) / nt;
-    const long long work = tiles * ((K + 63) / 64);
+    const long long bk = skinny_bk(M, nt);
+    const long long work = tiles * ((K + bk - 1) / bk);
     long long g = sms;
     if (g > work) g = work;
     if (g < 1) g = 1;
@@ -635,7 +659,7 @@ int skinny_env_nt() {
 SkinnyLayout skinny_layout(long long M, long long N, long long K, int sms, int nt_force) {
     SkinnyLayout L;
     int nt = nt_force;
-    L.slices = (nt == 0) ? skinny_lockstep_slices(N, K, sms) : 0;
+    L.slices = (nt == 0) ? skinny_lockstep_slices(M, N, K, sms) : 0;
     if (L.slices > 0) nt = 128;
     if (nt != 128 && nt != 256) nt = skinny_pick_nt(M, N, K, sms);
     L.nt = nt;
@@ -654,10 +678,10 @@ SkinnyLayout skinny_layout(long long M, long long N, long long K, int sms, int n
 size_t skinny_smem_bytes(long long M, int nt) {
     const int mp = skinny_mp(M);
     if (nt == 256)
-        return mp == 16 ? SkCfg<16, 256>::SMEM_BYTES : mp == 32 ? SkCfg<32, 256>::SMEM_BYTES
-                        : mp == 48 ? SkCfg<48, 256>::SMEM_BYTES : SkCfg<64, 256>::SMEM_BYTES;
-    return mp == 16 ? SkCfg<16, 128>::SMEM_BYTES : mp == 32 ? SkCfg<32, 128>::SMEM_BYTES
-                    : mp == 48 ? SkCfg<48, 128>::SMEM_BYTES : SkCfg<64, 128>::SMEM_BYTES;
+        return mp == 16 ? SkCfg<16, 256, 64>::SMEM_BYTES : mp == 32 ? SkCfg<32, 256, 64>::SMEM_BYTES
+                        : mp == 48 ? SkCfg<48, 256, 64>::SMEM_BYTES : SkCfg<64, 256, 64>::SMEM_BYTES;
+    return mp == 16 ? SkCfg<16, 128, 128>::SMEM_BYTES : mp == 32 ? SkCfg<32, 128, 128>::SMEM_BYTES
+                    : mp == 48 ? SkCfg<48, 128, 64>::SMEM_BYTES : SkCfg<64, 128, 64>::SMEM_BYTES;
 }
 
 // Epoch of the next launch (never 0).
@@ -671,23 +695,23 @@ unsigned long long skinny_last_epoch() { return g_skinny_epoch.load(); }
 
 int skinny_rotation_group();
 
-template <int MP, int NT>
+template <int MP, int NT, int BK>
 static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, float* ws,
                                        unsigned long long* flags, cudaStream_t stream) {
-    using Cfg = SkCfg<MP, NT>;
+    using Cfg = SkCfg<MP, NT, BK>;
     CUtensorMap tA, tB;
     const bool batched = pr.batch > 1;
     const bool za = batched && pr.sa > 0, zb = batched && pr.sb > 0;
     if (!sk_tmap(&tA, pr.A, pr.K, pr.M, pr.lda * 2, za ? pr.batch : 1, za ? pr.sa * 2 : 0, 64, MP))
         return PAX_ERR_CUDA;
-    if (!sk_tmap(&tB, pr.B, pr.N, pr.K, pr.ldb * 2, zb ? pr.batch : 1, zb ? pr.sb * 2 : 0, 64, 64))
+    if (!sk_tmap(&tB, pr.B, pr.N, pr.K, pr.ldb * 2, zb ? pr.batch : 1, zb ? pr.sb * 2 : 0, 64, BK))
         return PAX_ERR_CUDA;
     SkinnyParams p;
     p.M = (int)pr.M;
     p.N = (int)pr.N;
     p.K = (int)pr.K;
     p.num_tiles = (int)((pr.N + NT - 1) / NT);
-    p.kblocks = (int)((pr.K + 63) / 64);
+    p.kblocks = (int)((pr.K + BK - 1) / BK);
     p.work = (long long)p.num_tiles * p.kblocks;
     p.grid = grid;
     p.slices = slices;
@@ -722,7 +746,7 @@ static pax_status_t launch_skinny_impl(const Problem& pr, int grid, int slices, 
         return PAX_ERR_INVALID;
     }
     if (slices > 0 && slices * p.num_tiles != grid) return PAX_ERR_INVALID;
-    auto kern = gemm_skinny_kernel<MP, NT>;
+    auto kern = gemm_skinny_kernel<MP, NT, BK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES) != cudaSuccess)
         return PAX_ERR_CUDA;
     cudaLaunchConfig_t cfg = {};
@@ -743,10 +767,10 @@ template <int NT>
 static pax_status_t launch_skinny_nt(const Problem& p, int grid, int slices, float* ws,
                                      unsigned long long* flags, cudaStream_t stream) {
     switch (skinny_mp(p.M)) {
-        case 16: return launch_skinny_impl<16, NT>(p, grid, slices, ws, flags, stream);
-        case 32: return launch_skinny_impl<32, NT>(p, grid, slices, ws, flags, stream);
-        case 48: return launch_skinny_impl<48, NT>(p, grid, slices, ws, flags, stream);
-        default: return launch_skinny_impl<64, NT>(p, grid, slices, ws, flags, stream);
+        case 16: return launch_skinny_impl<16, NT, NT == 128 ? 128 : 64>(p, grid, slices, ws, flags, stream);
+        case 32: return launch_skinny_impl<32, NT, NT == 128 ? 128 : 64>(p, grid, slices, ws, flags, stream);
+        case 48: return launch_skinny_impl<48, NT, 64>(p, grid, slices, ws, flags, stream);
+        default: return launch_skinny_impl<64, NT, 64>(p, grid, slices, ws, flags, stream);
     }
 }
 

@@ -67,7 +67,7 @@ pax_status_t launch_simt(const Problem& p, cudaStream_t stream);
 // aborted, holds an older epoch.  skinny_geometry gives the grid and both
 // sizes; skinny_pick_nt the unit width.
 int skinny_pick_nt(long long M, long long N, long long K, int sms);
-int skinny_lockstep_slices(long long N, long long K, int sms);
+int skinny_lockstep_slices(long long M, long long N, long long K, int sms);
 void skinny_geometry(long long M, long long N, long long K, int sms, int nt, int* grid, size_t* ws_bytes,
                      size_t* flag_bytes);
 // The layout pax_gemm_ex runs for a skinny problem: nt, grid, K slices
