@@ -220,8 +220,9 @@ pax_status_t pax_gemm_ex(const pax_gemm_desc_t* desc, cudaStream_t stream);
  * return PAX_ERR_UNSUPPORTED with a message, before anything is launched.
  * The first call on a device (and the first after that device's CUDA
  * context was reset or re-created, or after pax_shutdown) looks up the
- * array's device address, so make it before any stream capture.  Each call
- * clears the counters it uses on `stream` first.  Each device has its own
+ * array's device address, so make it before any stream capture.  Nothing
+ * in the array needs clearing between calls: the split-tile publication
+ * flags hold a per-call 64-bit epoch.  Each device has its own
  * copy of the array, but all calls on one device share it: calls that
  * overlap on the GPU there (different streams without ordering between
  * them) race and give wrong results. */
@@ -383,8 +384,8 @@ pax_status_t pax_device_error(void);
  * usable.  For tests of the failure path; takes about 2 s of GPU time. */
 pax_status_t pax_selftest_bounded_wait(cudaStream_t stream);
 /* Test hook (new; no counterpart in the reference): writes into the skinny
- * kernel's split-K arrival counters of `stream`'s workspace (the current
- * device's) what a launch that gave up on a timed-out wait leaves behind.
+ * kernel's split-tile publication flags of `stream`'s workspace (the current
+ * device's) what launches that gave up on a timed-out wait leave behind.
  * The next skinny GEMM on that stream must still be correct.  Synchronises
  * `stream`.  PAX_ERR_INVALID if the stream has no workspace yet. */
 pax_status_t pax_selftest_stale_counters(cudaStream_t stream);

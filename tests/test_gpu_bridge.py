@@ -1,7 +1,7 @@
 """Host-bridge entry points on the GPU, through the C ABI: the reference's
 bench harness (src/host_bridge.c:543-566), the shared-memory queries of the
 reference-named launchers, and the skinny kernel's workspace handling
-(arrival counters left by an aborted launch, cudaStreamPerThread)."""
+(publication flags left by an aborted launch, cudaStreamPerThread)."""
 from __future__ import annotations
 
 import ctypes
@@ -67,13 +67,14 @@ def test_smem_queries_on_the_device(cuda):
     assert lib.pax_gemm_smem_bytes(ctypes.byref(d)) == lib.pax_gemm_ptx_smem_bytes()
 
 
-def test_skinny_ignores_counters_left_by_an_aborted_launch(cuda, rng):
-    """A launch that gave up on a timed-out wait can leave split-tile arrival
-    counters behind.  The next launch on that stream must ignore them (they
-    carry an older launch epoch) and still pick the right last arriver."""
+def test_skinny_ignores_flags_left_by_an_aborted_launch(cuda, rng):
+    """A launch that gave up on a timed-out wait can leave split-tile
+    publication flags behind.  The next launch on that stream must ignore
+    them (they carry an older launch epoch): its reducing CTAs must wait for
+    this launch's partial sums, not read stale ones."""
     s = torch.cuda.current_stream(cuda).cuda_stream
     # 32 column tiles: the lockstep layout splits each tile's K over 4 CTAs,
-    # so every tile uses an arrival counter.
+    # so every tile is reduced through flags; then stream-K.
     for M, N, K, nt in [(16, 4096, 4096, "0"), (16, 16384, 4096, "128")]:
         A, B = inputs(rng, M, N, K, dist="normal")
         ref = oracle.gemm(A, B, out_dtype=np.float16)
@@ -89,7 +90,7 @@ def test_skinny_ignores_counters_left_by_an_aborted_launch(cuda, rng):
 def test_per_thread_default_stream_from_two_threads(cuda, rng):
     """cudaStreamPerThread is one handle value that names a different stream
     in each host thread.  Skinny GEMMs on it from two threads at once must
-    not share a workspace (they would race on its counters and partials)."""
+    not share a workspace (they would race on its flags and partials)."""
     A, B = inputs(rng, 16, 4096, 4096, dist="normal")
     ref = oracle.gemm(A, B, out_dtype=np.float16)
     tA, tB = to_dev(A, cuda), to_dev(B, cuda)
