@@ -658,20 +658,25 @@ def split_record(args, dev, flush, peak, world, rank, local, steps, warmup, gath
         g = timed_steps(lambda: rc.gemm_slab(A, B, cfg["epi"], bias), steps, warmup, flush, dev, world, local)
         rec["replicated_fused"] = {"ms_per_step": g["max_over_ranks"],
                                    "tflops_total": flops / (g["max_over_ranks"] * 1e-3) / 1e12,
-                                   "bytes_pushed_per_rank": M * (s1 - s0) * 2 * (world - 1)}
+                                   "cost_vs_unreplicated": g["max_over_ranks"] / r["max_over_ranks"] - 1.0,
+                                   "bytes_pushed_per_rank": M * (s1 - s0) * 2 * (world - 1),
+                                   "ordering": rc.ordering}
         torch.cuda.synchronize()
         torch.distributed.barrier()
         rc.close()
         del rc
+        if pax_b200.device_error() != pax_b200.Status.OK:
+            raise RuntimeError("replicated C5: device-side wait timed out")
     del A, B, bias
     torch.cuda.empty_cache()
     return rec
 
 
 def gather_record(A, B, bias, res, cfg, M, N, n_total, dev, flush, world, local, steps, warmup):
-    """The C2 step with C replicated on every rank, two ways: the fused GEMM
-    + all-gather (epilogue TMA stores to every peer over NVLink, ordered by
-    two one-element all-reduces) and the GEMM followed by an NCCL
+    """The C2 step with C replicated on every rank, three ways: the fused
+    GEMM + all-gather (each finished tile copied to every peer's C over
+    NVLink while later tiles compute), ordered by peer flag barriers or by
+    two one-element NCCL all-reduces, and the GEMM followed by an NCCL
     all-gather of the slabs and a pack into row-major C."""
     import torch
     import torch.distributed as dist
@@ -680,13 +685,19 @@ def gather_record(A, B, bias, res, cfg, M, N, n_total, dev, flush, world, local,
     from pax_b200.dist import ReplicatedC, gather_columns
 
     flops = 2.0 * M * n_total * cfg["K"]
-    rc = ReplicatedC(M, n_total, device=dev)
     kb = bias if "bias" in cfg["epi"] else None
-    f = timed_steps(lambda: rc.gemm_slab(A, B, cfg["epi"], kb, res), steps, warmup, flush, dev, world, local)
-    torch.cuda.synchronize()
-    dist.barrier()
-    rc.close()
-    del rc
+    fused = {}
+    for ordering in ("flags", "collective"):
+        rc = ReplicatedC(M, n_total, device=dev, ordering=ordering)
+        fused[ordering] = timed_steps(lambda: rc.gemm_slab(A, B, cfg["epi"], kb, res), steps, warmup, flush, dev,
+                                      world, local)
+        torch.cuda.synchronize()
+        dist.barrier()
+        rc.close()
+        del rc
+        if pax_b200.device_error() != pax_b200.Status.OK:
+            raise RuntimeError(f"replicated C2 ({ordering} ordering): device-side wait timed out")
+    f = fused["flags"]
     C = torch.empty((M, N), dtype=torch.float16, device=dev)
 
     def nccl_step():
@@ -696,8 +707,13 @@ def gather_record(A, B, bias, res, cfg, M, N, n_total, dev, flush, world, local,
     n = timed_steps(nccl_step, steps, warmup, flush, dev, world, local)
     torch.cuda.empty_cache()
     slab = M * N * 2
+    c = fused["collective"]
     return {"fused": {"ms_per_step": f["max_over_ranks"], "tflops_total": flops / (f["max_over_ranks"] * 1e-3) / 1e12,
-                      "how": "epilogue TMA stores to every peer's C over NVLink + 2 one-element NCCL all-reduces"},
+                      "how": "each finished tile TMA-copied from the local C to every peer's C over NVLink while "
+                             "later tiles compute; a peer flag barrier (pax_peer_barrier) before and after"},
+            "fused_nccl_ordering": {"ms_per_step": c["max_over_ranks"],
+                                    "tflops_total": flops / (c["max_over_ranks"] * 1e-3) / 1e12,
+                                    "how": "the same kernel, ordered by 2 one-element NCCL all-reduces"},
             "nccl": {"ms_per_step": n["max_over_ranks"], "tflops_total": flops / (n["max_over_ranks"] * 1e-3) / 1e12,
                      "how": "GEMM, then NCCL all_gather_into_tensor of the slabs and a pack into row-major C"},
             "bytes_per_rank_to_peers": slab * (world - 1)}

@@ -250,11 +250,28 @@ pax_status_t pax_gemm_batched_ex(const pax_gemm_batched_desc_t* desc, cudaStream
  * of other GPUs' C buffers mapped with pax_ipc_import.  The copies travel
  * over NVLink while the kernel computes later tiles.  Each replica receives
  * complete, system-visible data once the kernel has finished; a reader on
- * another GPU must order its reads after that (for example, by a collective
- * on the same streams).  Tensor-core path only (m > 64, 16-byte aligned
+ * another GPU must order its reads after that (pax_peer_barrier, or a
+ * collective on the same streams).  The copies to the replicas are made
+ * after each tile's local store, from the local C, so C itself must not be
+ * written by anyone else while the kernel runs.  Tensor-core path only (m > 64, 16-byte aligned
  * rows): other problems return PAX_ERR_UNSUPPORTED. */
 pax_status_t pax_gemm_replicated_ex(const pax_gemm_desc_t* desc, void* const* replicas, int n_replicas,
                                    cudaStream_t stream);
+
+/* Rank barrier for replicated outputs, over NVLink peer memory (new; it
+ * replaces a collective as the ordering around pax_gemm_replicated_ex).
+ * `own` is this rank's array of n_peers + 1 64-bit flags in device memory,
+ * zero when created; peers[i] are the other ranks' arrays, mapped with
+ * pax_ipc_import; `slot` is this rank's index in every array.  One small
+ * kernel on `stream`, after everything queued before it there, release-
+ * stores `epoch` into slot `slot` of every peer's array, then waits until
+ * every other slot of `own` holds at least `epoch`.  Work queued after it
+ * therefore starts only when every rank has reached the barrier.  Epochs must
+ * grow from call to call, the same sequence on every rank (nothing is ever
+ * cleared).  A wait longer than timeout_ns (0: 10 s) gives up and records a
+ * timeout that pax_device_error() returns as PAX_ERR_TIMEOUT. */
+pax_status_t pax_peer_barrier(unsigned long long* own, unsigned long long* const* peers, int n_peers, int slot,
+                              unsigned long long epoch, unsigned long long timeout_ns, cudaStream_t stream);
 
 /* CUDA IPC handle of the allocation holding a device pointer, plus the
  * pointer's offset in it (new).  pax_ipc_import maps it in another process

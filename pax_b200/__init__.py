@@ -10,12 +10,12 @@ LibraryNotBuilt; there is no CPU fallback.
 from . import _lib
 from ._lib import LIB_PATH, GemmDesc, LibraryNotBuilt, PaxBuffer
 from .api import (Algo, DType, Epilogue, PaxError, Status, device_error, gemm, gemm_batched, ipc_close, ipc_export,
-                  ipc_import, last_error, make_desc, pipeline_stages, select_algo)
+                  ipc_import, last_error, make_desc, peer_barrier, pipeline_stages, select_algo)
 
 __all__ = [
     "LIB_PATH", "GemmDesc", "LibraryNotBuilt", "PaxBuffer", "lib", "Algo", "DType", "Epilogue", "PaxError",
     "Status", "device_error", "gemm", "gemm_batched", "ipc_close", "ipc_export", "ipc_import", "last_error",
-    "make_desc", "pipeline_stages", "select_algo",
+    "make_desc", "peer_barrier", "pipeline_stages", "select_algo",
 ]
 
 

@@ -102,6 +102,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "pax_ipc_export": ([P, ctypes.POINTER(IpcHandle)], i),
         "pax_ipc_import": ([ctypes.POINTER(IpcHandle), ctypes.POINTER(P)], i),
         "pax_ipc_close": ([P], i),
+        "pax_peer_barrier": ([P, ctypes.POINTER(P), i, i, u64, u64, P], i),
         "pax_gemm_select_algo": ([ctypes.POINTER(GemmDesc)], i),
         "pax_gemm_pipeline_stages": ([ctypes.POINTER(GemmDesc)], i),
         "pax_gemm_smem_bytes": ([ctypes.POINTER(GemmDesc)], sz),

@@ -218,6 +218,20 @@ def ipc_close(ptr: int) -> None:
         raise PaxError(st, "pax_ipc_close")
 
 
+def peer_barrier(own: int, peers: list[int], slot: int, epoch: int, timeout_ns: int = 0,
+                 stream: torch.cuda.Stream | None = None) -> None:
+    """pax_peer_barrier on `stream` (default: the current stream): signal
+    `epoch` into slot `slot` of every peer's flag array, then wait until
+    every other slot of `own` holds at least `epoch`.  Addresses are device
+    pointers (the peers' mapped with ipc_import)."""
+    s = stream if stream is not None else torch.cuda.current_stream()
+    arr = (ctypes.c_void_p * max(1, len(peers)))(*peers)
+    st = _lib.get().pax_peer_barrier(ctypes.c_void_p(own), arr, len(peers), slot, epoch, timeout_ns,
+                                     ctypes.c_void_p(s.cuda_stream))
+    if st != 0:
+        raise PaxError(st, "pax_peer_barrier")
+
+
 def device_error() -> Status:
     """Read and clear the device error word (synchronises the device)."""
     return Status(_lib.get().pax_device_error())

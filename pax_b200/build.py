@@ -21,8 +21,8 @@ LIB = os.path.join(HERE, "libpax_b200.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
-SOURCES = ["gemm_tc_f16.cu", "gemm_tc_f32.cu", "gemm_tc.cu", "gemm_skinny.cu", "gemm_simt.cu", "host_bridge.cpp",
-           "fp16_ops.cpp"]
+SOURCES = ["gemm_tc_f16.cu", "gemm_tc_f32.cu", "gemm_tc.cu", "gemm_skinny.cu", "gemm_simt.cu", "peer_sync.cu",
+           "host_bridge.cpp", "fp16_ops.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr", "-I", INCLUDE]
 # Host-only translation unit: cpu_gemm_ref is built with the same host flags

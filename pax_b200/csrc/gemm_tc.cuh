@@ -140,7 +140,9 @@ struct TcCfg {
     static constexpr uint32_t STG_TOTAL = EPI_WARPS * STG_BYTES;
     static constexpr int ACC_BUFS = WIDE ? 1 : 2;        // accumulator buffers in TMEM
     static constexpr uint32_t TMEM_COLS = ACC_BUFS * BN;
-    static constexpr uint32_t NUM_BARS = 2 * STAGES + 5;
+    // full[STAGES], empty[STAGES], tfull[2], tempty[2], drain, and one per
+    // epilogue warp for the reloads of its replica pushes.
+    static constexpr uint32_t NUM_BARS = 2 * STAGES + 5 + EPI_WARPS;
     static constexpr size_t SMEM_BYTES =
         1024 + (size_t)STAGES * STAGE_BYTES + STG_TOTAL + NUM_BARS * 8 + 16;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -210,6 +212,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     const uint32_t tfull0 = bar0 + 16u * STAGES;     // [2]
     const uint32_t tempty0 = tfull0 + 16u;           // [2]
     const uint32_t drain_bar = tempty0 + 16u;
+    const uint32_t push0 = drain_bar + 8u;           // [EPI_WARPS]
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -236,6 +239,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             mbar_init(tempty0 + 8u * b, PAIR ? 2 * Cfg::EPI_WARPS : Cfg::EPI_WARPS);
         }
         mbar_init(drain_bar, 1);
+        for (int w = 0; w < Cfg::EPI_WARPS; ++w) mbar_init(push0 + 8u * w, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -431,6 +435,8 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         uint8_t* sbuf = sStg + (warp - 2) * Cfg::STG_BYTES;
         // C much larger than L2 passes through it once.
         const uint64_t pol_stream = l2_evict_first_policy();
+        const uint32_t pbar = push0 + 8u * (uint32_t)(warp - 2);
+        uint32_t push_phase = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int k = k_begin; k < k_end; k += k_step) {
@@ -523,10 +529,32 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         tma_store_3d_hint(&tmC, smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz, pol_stream);
                     else
                         tma_store_3d(&tmC, smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz);
-                    for (int d = 0; d < reps.n; ++d)
-                        tma_store_3d(&reps.map[d], smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz);
                     bulk_commit();
                 }
+            }
+            // Replicas: once the accumulator is handed back, this warp copies
+            // its finished chunks from the local C to every replica, one chunk
+            // at a time through its staging buffer (TMA load from this GPU's
+            // memory, then one TMA store per replica).  The pushes overlap the
+            // next item's MMAs instead of holding up this epilogue; NVLink
+            // bandwidth then limits only the last item's pushes.
+            if (reps.n > 0 && nch > 0) {
+                if (lane == 0) {
+                    bulk_wait<0>();  // the local stores of this item are complete
+#pragma unroll 1
+                    for (int ci = 0; ci < nch; ++ci) {
+                        const int col = (int)(tcol0 + ci * EC);
+                        bulk_wait_read<0>();  // the previous chunk's pushes have read the buffer
+                        mbar_arrive_expect_tx(pbar, Cfg::STG_BYTES);
+                        tma_load_3d(smem_u32(sbuf), &tmC, pbar, col, row0, bz);
+                        const bool landed = mbar_wait(pbar, push_phase, nullptr);
+                        push_phase ^= 1u;
+                        if (!landed) break;  // timed out: error recorded, the load has had 2 s
+                        for (int d = 0; d < reps.n; ++d) tma_store_3d(&reps.map[d], smem_u32(sbuf), col, row0, bz);
+                        bulk_commit();
+                    }
+                }
+                __syncwarp();
             }
             if (++acc == Cfg::ACC_BUFS) {
                 acc = 0;

@@ -436,8 +436,9 @@ pax_status_t pax_device_error(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return set_status(PAX_ERR_CUDA);
     const int a = read_clear_device_error_tc();
     const int b = read_clear_device_error_skinny();
-    if (a < 0 || b < 0) return set_status(PAX_ERR_CUDA);
-    return set_status((a | b) ? PAX_ERR_TIMEOUT : PAX_OK);
+    const int c = read_clear_device_error_peer();
+    if (a < 0 || b < 0 || c < 0) return set_status(PAX_ERR_CUDA);
+    return set_status((a | b | c) ? PAX_ERR_TIMEOUT : PAX_OK);
 }
 
 void pax_shutdown(void) {
@@ -487,6 +488,24 @@ pax_status_t pax_gemm_replicated_ex(const pax_gemm_desc_t* desc, void* const* re
     p.replicas = replicas;
     p.n_replicas = n_replicas;
     return run(p, algo_of(desc), stream);
+}
+
+pax_status_t pax_peer_barrier(unsigned long long* own, unsigned long long* const* peers, int n_peers, int slot,
+                              unsigned long long epoch, unsigned long long timeout_ns, cudaStream_t stream) {
+    if (n_peers < 0 || n_peers > kPeerMaxPeers)
+        return fail(PAX_ERR_INVALID, "pax_peer_barrier: %d peers (0..%d allowed)", n_peers, kPeerMaxPeers);
+    if (slot < 0 || slot > n_peers)
+        return fail(PAX_ERR_INVALID, "pax_peer_barrier: slot %d outside the %d ranks", slot, n_peers + 1);
+    if (!own || (reinterpret_cast<uintptr_t>(own) & 7u) || (n_peers > 0 && !peers))
+        return fail(PAX_ERR_INVALID, "pax_peer_barrier: own flags NULL or not 8-byte aligned");
+    for (int i = 0; i < n_peers; ++i)
+        if (!peers[i] || (reinterpret_cast<uintptr_t>(peers[i]) & 7u))
+            return fail(PAX_ERR_INVALID, "pax_peer_barrier: peer %d flags NULL or not 8-byte aligned", i);
+    if (epoch == 0) return fail(PAX_ERR_INVALID, "pax_peer_barrier: epoch 0 (flags start at 0)");
+    const unsigned long long limit = timeout_ns ? timeout_ns : 10000000000ull;
+    if (peer_barrier_launch(own, peers, n_peers, slot, epoch, limit, stream) != cudaSuccess)
+        return fail(PAX_ERR_CUDA, "pax_peer_barrier: launch failed");
+    return set_status(PAX_OK);
 }
 
 // ------------------------------------------------------------- CUDA IPC

@@ -123,6 +123,12 @@ pax_status_t report_status(pax_status_t s, const char* msg);
 // the current device.
 int read_clear_device_error_tc();
 int read_clear_device_error_skinny();
+int read_clear_device_error_peer();
+
+// Rank barrier over peer memory (peer_sync.cu, pax_peer_barrier).
+constexpr int kPeerMaxPeers = 7;
+cudaError_t peer_barrier_launch(unsigned long long* own, unsigned long long* const* peers, int n_peers, int slot,
+                                unsigned long long epoch, unsigned long long limit_ns, cudaStream_t stream);
 // Set the limit of the kernels' abandonable waits on the current device
 // (pax_selftest_set_wait_limit).
 bool set_wait_limit_tc(unsigned long long ns);

@@ -78,9 +78,14 @@ class ReplicatedC:
     peer's C while the kernel goes on with later tiles.  Stores only: no
     kernel reads another GPU's memory.
 
-    Ordering: a one-element all-reduce before the kernel (every rank has
-    finished reading the previous contents) and one after it (every rank's
-    slab has landed everywhere) bracket each call, on the current stream.
+    Ordering: a rank barrier before the kernel (every rank has finished
+    reading the previous contents) and one after it (every rank's slab has
+    landed everywhere) bracket each call, on the current stream.  With
+    ``ordering="flags"`` (the default for CUDA buffers) each barrier is
+    pax_peer_barrier: one small kernel that release-stores an epoch into the
+    peers' flag arrays over NVLink and waits, bounded, for theirs.  With
+    ``ordering="collective"`` (the default elsewhere) it is a one-element
+    all-reduce of the process group.
 
     With a `monitor` (a PeerMonitor), each call first checks on the host
     that every peer is alive and at the same step, and raises RankFailure
@@ -91,8 +96,9 @@ class ReplicatedC:
     """
 
     def __init__(self, M: int, N_total: int, dtype: torch.dtype = torch.float16, device=None, group=None, *,
-                 monitor: PeerMonitor | None = None, _export: Callable | None = None,
-                 _import: Callable | None = None, _close: Callable | None = None):
+                 monitor: PeerMonitor | None = None, ordering: str | None = None, barrier_timeout_ns: int = 0,
+                 _export: Callable | None = None, _import: Callable | None = None, _close: Callable | None = None,
+                 _barrier: Callable | None = None):
         from . import api
 
         self.group = group
@@ -101,8 +107,28 @@ class ReplicatedC:
         self.rank = dist.get_rank(group)
         if not equal_slabs(N_total, self.world):
             raise ValueError("replicated C needs N_total divisible by 8 * ranks")
-        self.full = torch.empty((M, N_total), dtype=dtype, device=device)
+        if ordering is None:
+            ordering = "flags" if torch.device(device if device is not None else "cpu").type == "cuda" else \
+                "collective"
+        if ordering not in ("flags", "collective"):
+            raise ValueError(f"ordering must be 'flags' or 'collective', not {ordering!r}")
+        self.ordering = ordering
+        self.barrier_timeout_ns = int(barrier_timeout_ns)
+        # One allocation holds C and, after it, this rank's barrier flags (one
+        # 64-bit slot per rank), so a peer maps both with one IPC handle.  The
+        # flags are zero before any peer can see them: the fill completes
+        # before the handles are exchanged.
+        c_bytes = M * N_total * torch.empty((), dtype=dtype).element_size()
+        self.sync_offset = (c_bytes + 255) // 256 * 256
+        buf = torch.empty(self.sync_offset + 8 * self.world, dtype=torch.uint8, device=device)
+        self.full = buf[:c_bytes].view(dtype).view(M, N_total)
+        self.sync = buf[self.sync_offset:].view(torch.int64)
+        self.sync.zero_()
+        if self.sync.is_cuda:
+            torch.cuda.current_stream(self.sync.device).synchronize()
+        self._epoch = 0
         self._close = _close or api.ipc_close
+        self._barrier_fn = _barrier or api.peer_barrier
         mine = (_export or api.ipc_export)(self.full)
         handles: list = [None] * self.world
         dist.all_gather_object(handles, mine, group=group)
@@ -133,11 +159,21 @@ class ReplicatedC:
         s, e = self.slab
         if self.monitor is not None:
             self.monitor.step()
-        dist.all_reduce(self._flag, group=self.group)
+        self.barrier()
         gemm_fn(A, B_slab, epilogue=epilogue, bias=bias_slab, residual=residual_slab, out=self.full[:, s:e],
                 replicas=self.replica_addresses())
-        dist.all_reduce(self._flag, group=self.group)
+        self.barrier()
         return self.full
+
+    def barrier(self) -> None:
+        """Every rank's work queued on its current stream before this point
+        is complete before anything queued after it runs (on every rank)."""
+        if self.ordering == "collective":
+            dist.all_reduce(self._flag, group=self.group)
+            return
+        self._epoch += 1
+        peers = [base + self.sync_offset for _, base in sorted(self.peers.items())]
+        self._barrier_fn(self.sync.data_ptr(), peers, self.rank, self._epoch, self.barrier_timeout_ns)
 
     def close(self) -> None:
         for ptr in self.peers.values():

@@ -305,6 +305,26 @@ def test_ipc_helpers_reject_bad_arguments():
     assert lib.pax_ipc_close(ctypes.c_void_p(0x1234)) == pax_b200.Status.INVALID  # never imported
 
 
+def test_peer_barrier_rejects_bad_arguments():
+    """pax_peer_barrier checks its arguments on the host, before any launch."""
+    lib = pax_b200.lib
+    P = ctypes.c_void_p
+    own = P(0x10000)
+    peers = (P * 8)(*[0x20000 + 0x1000 * i for i in range(8)])
+    INVALID = pax_b200.Status.INVALID
+    assert lib.pax_peer_barrier(own, peers, 8, 0, 1, 0, None) == INVALID  # more than 7 peers
+    assert lib.pax_peer_barrier(own, peers, -1, 0, 1, 0, None) == INVALID
+    assert lib.pax_peer_barrier(own, peers, 1, 2, 1, 0, None) == INVALID  # slot outside 2 ranks
+    assert lib.pax_peer_barrier(own, peers, 1, -1, 1, 0, None) == INVALID
+    assert lib.pax_peer_barrier(None, peers, 1, 0, 1, 0, None) == INVALID
+    assert lib.pax_peer_barrier(P(0x10004), peers, 1, 0, 1, 0, None) == INVALID  # not 8-byte aligned
+    assert lib.pax_peer_barrier(own, None, 1, 0, 1, 0, None) == INVALID
+    bad = (P * 2)(0x20000, 0x20003)
+    assert lib.pax_peer_barrier(own, bad, 2, 0, 1, 0, None) == INVALID
+    assert lib.pax_peer_barrier(own, peers, 1, 0, 0, 0, None) == INVALID  # epoch 0
+    assert lib.pax_last_error() == INVALID
+
+
 def test_status_strings_and_version():
     for s in pax_b200.Status:
         assert lib.pax_status_string(int(s))

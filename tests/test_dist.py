@@ -155,3 +155,88 @@ def test_replicated_c_host_logic(world):
         assert out_off == r * Ns * 2 and tuple(out_shape) == (M, Ns) and out_stride == (N, 1)  # bytes
         expect = [((p + 1) << 40) + r * Ns * 2 for p in range(world) if p != r]
         assert replicas == expect
+
+
+def _flags_worker(rank, world, port, M, N, K, q):
+    """ReplicatedC with flag ordering, with stand-ins for IPC and the
+    barrier kernel: every call is bracketed by two barriers with growing
+    epochs, each given this rank's flag array, the peers' mapped arrays in
+    rank order and this rank as the slot; close unmaps C and flags."""
+    from pax_b200.dist import ReplicatedC
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        events, closed = [], []
+
+        def fake_gemm(A, B, *, epilogue, bias, residual, out, replicas):
+            events.append(("gemm",))
+
+        def fake_barrier(own, peers, slot, epoch, timeout_ns):
+            events.append(("barrier", own == rc.sync.data_ptr(), list(peers), slot, epoch, timeout_ns))
+
+        # The fake mapping puts rank r's C at (r + 1) << 40; its flags follow
+        # C in the same allocation.
+        rc = ReplicatedC(M, N, device="cpu", ordering="flags", barrier_timeout_ns=5_000_000,
+                         _export=lambda t: str(dist.get_rank()).encode(),
+                         _import=lambda h: (int(h.decode()) + 1) << 40, _close=closed.append, _barrier=fake_barrier)
+        assert rc.sync_offset % 256 == 0 and rc.sync_offset >= M * N * 2
+        assert rc.sync.data_ptr() - rc.full.data_ptr() == rc.sync_offset and rc.sync.tolist() == [0] * world
+        A = torch.zeros((M, K), dtype=torch.float16)
+        B = torch.zeros((K, N), dtype=torch.float16)
+        for _ in range(2):
+            rc.gemm(A, B, gemm_fn=fake_gemm)
+        off = rc.sync_offset
+        rc.close()
+        q.put((rank, events, sorted(closed), off))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_replicated_c_flag_ordering_host_logic(world):
+    M, N, K = 8, 16 * world, 16
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_flags_worker, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    deadline = time.time() + 180
+    while len(got) < world and time.time() < deadline:
+        try:
+            r, events, closed, off = q.get(timeout=1)
+            got[r] = (events, closed, off)
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in procs):
+                break
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert len(got) == world, f"ranks failed: {[p.exitcode for p in procs]}"
+    for r, (events, closed, off) in got.items():
+        peer_flags = [((p + 1) << 40) + off for p in range(world) if p != r]
+        kinds = [e[0] for e in events]
+        assert kinds == ["barrier", "gemm", "barrier"] * 2
+        barriers = [e for e in events if e[0] == "barrier"]
+        assert [b[4] for b in barriers] == [1, 2, 3, 4]  # epochs grow, the same on every rank
+        for _, own_ok, peers, slot, _, timeout_ns in barriers:
+            assert own_ok and peers == peer_flags and slot == r and timeout_ns == 5_000_000
+        assert closed == [(p + 1) << 40 for p in range(world) if p != r]  # one mapping per peer
+
+
+def test_replicated_c_rejects_unknown_ordering():
+    from pax_b200.dist import ReplicatedC
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(_free_port())
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        with pytest.raises(ValueError, match="ordering"):
+            ReplicatedC(8, 16, device="cpu", ordering="nccl", _export=lambda t: b"h", _import=lambda h: 1 << 40,
+                        _close=lambda p: None)
+    finally:
+        dist.destroy_process_group()

@@ -120,3 +120,38 @@ def test_per_thread_default_stream_from_two_threads(cuda, rng):
         t.join()
     assert not errors, errors
     assert pax_b200.device_error() == pax_b200.Status.OK
+
+
+def test_peer_barrier_on_one_gpu(cuda):
+    """pax_peer_barrier with both ranks' flag arrays on this GPU: rank 0's
+    barrier signals its epoch into the peer's array and passes once rank 1's
+    slot of its own array holds that epoch or a later one."""
+    own = torch.zeros(2, dtype=torch.int64, device=cuda)
+    peer = torch.zeros(2, dtype=torch.int64, device=cuda)
+    own[1] = 5  # rank 1 has already reached epoch 5
+    torch.cuda.synchronize()
+    for epoch in (3, 5):
+        pax_b200.peer_barrier(own.data_ptr(), [peer.data_ptr()], 0, epoch, timeout_ns=1_000_000_000)
+        torch.cuda.synchronize()
+        assert peer.cpu().tolist() == [epoch, 0]
+    assert own.cpu().tolist() == [0, 5]
+    assert pax_b200.device_error() == pax_b200.Status.OK
+
+
+def test_peer_barrier_times_out_without_the_peer(cuda):
+    """A peer that never signals: the barrier's wait gives up after its
+    limit, the timeout is reported once, and the device keeps working."""
+    own = torch.zeros(2, dtype=torch.int64, device=cuda)
+    peer = torch.zeros(2, dtype=torch.int64, device=cuda)
+    torch.cuda.synchronize()
+    pax_b200.peer_barrier(own.data_ptr(), [peer.data_ptr()], 0, 1, timeout_ns=2_000_000)
+    torch.cuda.synchronize()
+    assert peer.cpu().tolist() == [1, 0]
+    assert pax_b200.device_error() == pax_b200.Status.TIMEOUT
+    assert pax_b200.device_error() == pax_b200.Status.OK
+    A = torch.randn((256, 128), device=cuda).half()
+    B = torch.randn((128, 256), device=cuda).half()
+    C = pax_b200.gemm(A, B)
+    torch.cuda.synchronize()
+    ref = (A.float() @ B.float()).half()
+    assert torch.allclose(C.float(), ref.float(), rtol=2e-2, atol=2e-2)

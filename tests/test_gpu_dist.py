@@ -40,14 +40,17 @@ def _rank(rank, world, port, M, N, K, q):
         bias = torch.randn((N,), generator=g).half()
         C_slab = local_slab_gemm(A.to(dev), B.to(dev), rank, world, epilogue="bias_gelu_tanh", bias=bias.to(dev))
         C = gather_columns(C_slab)
-        # Fused: each rank's kernel also stores its slab into the peer's C.
-        rc = ReplicatedC(M, N, device=dev)
+        # Fused: each rank's kernel also copies its slab into the peer's C,
+        # ordered by peer flag barriers, then by NCCL all-reduces.
         fused = []
-        for _ in range(2):  # the second call overwrites the same buffers
-            rc.full.zero_()
-            fused.append(rc.gemm(A.to(dev), B.to(dev), "bias_gelu_tanh", bias=bias.to(dev)).cpu().numpy())
-        torch.cuda.synchronize()
-        rc.close()
+        for ordering in ("flags", "collective"):
+            rc = ReplicatedC(M, N, device=dev, ordering=ordering, barrier_timeout_ns=20_000_000_000)
+            for _ in range(3):  # later calls overwrite the same buffers
+                rc.full.zero_()
+                fused.append(rc.gemm(A.to(dev), B.to(dev), "bias_gelu_tanh", bias=bias.to(dev)).cpu().numpy())
+            torch.cuda.synchronize()
+            dist.barrier()
+            rc.close()
         q.put((rank, C.cpu().numpy(), int(pax_b200.device_error()), fused))
         dist.barrier()
     finally:
