@@ -140,9 +140,10 @@ struct TcCfg {
     static constexpr uint32_t STG_TOTAL = EPI_WARPS * STG_BYTES;
     static constexpr int ACC_BUFS = WIDE ? 1 : 2;        // accumulator buffers in TMEM
     static constexpr uint32_t TMEM_COLS = ACC_BUFS * BN;
-    // full[STAGES], empty[STAGES], tfull[2], tempty[2], drain, and one per
-    // epilogue warp for the reloads of its replica pushes.
-    static constexpr uint32_t NUM_BARS = 2 * STAGES + 5 + EPI_WARPS;
+    // full[STAGES], empty[STAGES], tfull[2], tempty[2], drain, one per
+    // epilogue warp for the reloads of its replica pushes, and (pair) the
+    // non-leader's report of how many k-blocks it issued.
+    static constexpr uint32_t NUM_BARS = 2 * STAGES + 6 + EPI_WARPS;
     static constexpr size_t SMEM_BYTES =
         1024 + (size_t)STAGES * STAGE_BYTES + STG_TOTAL + NUM_BARS * 8 + 16;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -205,6 +206,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(sStg + Cfg::STG_TOTAL);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NUM_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile uint32_t* issued_slot = tmem_slot + 2;  // pair: the non-leader's k-block count
 
     const uint32_t bar0 = smem_u32(bars);
     const uint32_t full0 = bar0;                     // [STAGES]
@@ -213,6 +215,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     const uint32_t tempty0 = tfull0 + 16u;           // [2]
     const uint32_t drain_bar = tempty0 + 16u;
     const uint32_t push0 = drain_bar + 8u;           // [EPI_WARPS]
+    const uint32_t report_bar = push0 + 8u * Cfg::EPI_WARPS;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -240,6 +243,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         }
         mbar_init(drain_bar, 1);
         for (int w = 0; w < Cfg::EPI_WARPS; ++w) mbar_init(push0 + 8u * w, 1);
+        mbar_init(report_bar, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -273,6 +277,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             uint32_t phase = 0;
             bool ok = true;
             uint32_t issued = 0, last_parity = 0;
+            int total = 0;  // k-blocks issued by this CTA
             for (int k = k_begin; ok && k < k_end; k += k_step) {
                 const TcWork wk = tc_work<BN>(k, p, items);
                 const int za = p.za ? wk.bz : 0, zb = p.zb ? wk.bz : 0;
@@ -312,6 +317,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         for (int j = 0; j < l1 / 64; ++j)
                             tma_load_3d(bdst + (l0 / 64 + j) * 8192, &tmB, fb, c1 + j * 64, kb * Cfg::BK, zb);
                     }
+                    ++total;
                     issued |= 1u << stage;
                     last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
@@ -320,17 +326,49 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     }
                 }
             }
-            if (!ok) {
-                // Abort: every TMA load issued must land before the CTA exits.
-                if (!PAIR || leader) {
-                    for (int s = 0; s < STAGES; ++s)
-                        if (issued & (1u << s)) mbar_wait(full0 + 8u * s, (last_parity >> s) & 1u, nullptr);
+            if constexpr (PAIR) {
+                // Every TMA load either CTA issued must land before the pair
+                // tears down.  They all complete on the leader's full
+                // barriers, so the non-leader reports how many k-blocks it
+                // issued, and the leader settles the last phase of every
+                // stage: a phase only one CTA contributed to is completed
+                // for the other (its bytes cancelled, or the phase armed for
+                // the non-leader's bytes alone), then waited for.  Both CTAs
+                // issue the same k-block sequence, gated by the same slot
+                // releases, so neither is more than STAGES k-blocks ahead.
+                // After a normal run every phase has already completed.  The
+                // non-leader leaves only at the final cluster barrier, after
+                // these waits.
+                if (!leader) {
+                    st_shared_cluster_u32(smem_u32((const void*)issued_slot), 0, (uint32_t)total);
+                    mbar_arrive_cluster(report_bar, 0);
                 } else {
-                    // The peer's loads complete on the leader's barriers, which
-                    // this CTA cannot wait on: give them ample time to land.
-                    const unsigned long long t0 = globaltimer_ns();
-                    while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+                    // The non-leader reports when its own loop ends, at the
+                    // latest one abandonable wait later.
+                    bool reported = mbar_wait<true>(report_bar, 0, nullptr);
+                    if (!reported) reported = mbar_wait<true>(report_bar, 0, nullptr);
+                    const int t_nl = reported ? (int)*issued_slot : total;
+                    const int t_max = total > t_nl ? total : t_nl;
+                    for (int s = 0; s < STAGES; ++s) {
+                        if (t_max <= s) break;
+                        const int i = s + ((t_max - 1 - s) / STAGES) * STAGES;  // last k-block on stage s
+                        const bool mine = i < total, theirs = i < t_nl;
+                        if (mine != theirs) {
+                            const TcWork wk = tc_work<BN>(k_begin + (i / num_kb) * k_step, p, items);
+                            const int n0 = wk.w < 256 ? wk.w : 256, n1 = Cfg::WIDE ? wk.w - n0 : 0;
+                            const uint32_t half = Cfg::A_BYTES + (uint32_t)(n0 / 2 + n1 / 2) * Cfg::BK * 2;
+                            if (mine)
+                                mbar_complete_tx(full0 + 8u * s, half);  // the non-leader's half never comes
+                            else
+                                mbar_arrive_expect_tx(full0 + 8u * s, half);  // only the non-leader's half
+                        }
+                        mbar_wait(full0 + 8u * s, (uint32_t)(i / STAGES) & 1u, nullptr);
+                    }
                 }
+            } else if (!ok) {
+                // Abort: every TMA load issued must land before the CTA exits.
+                for (int s = 0; s < STAGES; ++s)
+                    if (issued & (1u << s)) mbar_wait(full0 + 8u * s, (last_parity >> s) & 1u, nullptr);
             }
         }
     } else if (warp == 1) {

@@ -615,12 +615,17 @@ pax_algo_t pax_gemm_select_algo(const pax_gemm_desc_t* desc) {
     if (normalize(desc, &p) != PAX_OK) return PAX_ALGO_AUTO;
     set_status(PAX_OK);
     pax_algo_t a = select_algo(p);
-    // With a device present, report the tensor-core tile shape as well.
+    // With a device present, report the tensor-core tile shape as well: the
+    // kernel pax_gemm_ex would launch (CTA pair or not), shape switches
+    // included.
     int dev = 0, sms = 0;
     if (a == PAX_ALGO_TC && cudaGetDevice(&dev) == cudaSuccess &&
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0 &&
-        (tc_pick_shape(p, sms) == 2 || tc_pick_shape(p, sms) == 4))
-        a = PAX_ALGO_TC2;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0) {
+        pax_algo_t b = PAX_ALGO_AUTO;
+        int shape = 0;
+        choose_kernel(p, sms, &b, &shape);
+        a = b;
+    }
     cudaGetLastError();  // no device here is not an error of this call
     return a;
 }

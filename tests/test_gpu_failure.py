@@ -44,8 +44,9 @@ def test_bounded_wait_times_out_and_context_survives(cuda, rng):
 # takes its abort path: its issued TMA loads land, its issued MMAs drain,
 # TMEM is freed, a timeout is recorded, and it ends.  Nothing faults or hangs:
 # the abort path's own waits keep the 2 s limit.  The next GEMM in the same
-# context must be correct.  The CTA-pair kernels are not driven into their
-# abort path here.
+# context must be correct.  In the CTA-pair kernels both CTAs' loads complete
+# on the leader's barriers; the non-leader reports how many k-blocks it
+# issued and the leader settles every stage before the pair tears down.
 SHORT_NS = 2000
 
 
@@ -63,7 +64,7 @@ def _abort_run(fn):
 
 @pytest.mark.parametrize("shape", ["128", "256"])
 def test_tc_one_cta_kernel_abort_path(cuda, rng, monkeypatch, shape):
-    monkeypatch.setenv("PAX_TC_SHAPE", shape)
+    monkeypatch.setenv("PAX_TC_BN", shape)
     g = torch.Generator(device=cuda)
     g.manual_seed(7)
     A = torch.randn((1024, 65536), generator=g, device=cuda).half()
@@ -78,6 +79,29 @@ def test_tc_one_cta_kernel_abort_path(cuda, rng, monkeypatch, shape):
     A2, B2 = inputs(rng, 640, 1024, 512)
     b2 = rng.standard_normal(1024).astype(np.float16)
     got = run_gemm(A2, B2, cuda, epi="bias_gelu_tanh", bias=b2, out_dtype=np.float16, algo="tc")
+    check(got, oracle.gemm(A2, B2, epi="bias_gelu_tanh", bias=b2, out_dtype=np.float16), np.float16)
+    assert pax_b200.device_error() == pax_b200.Status.OK
+
+
+@pytest.mark.parametrize("shape", ["2", "4"])
+def test_tc_pair_kernel_abort_path(cuda, rng, monkeypatch, shape):
+    # 2: CTA pairs on 256 x 256 tiles; 4: CTA pairs on 256 x 512 tiles.
+    monkeypatch.setenv("PAX_TC_SHAPE", shape)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(9)
+    A = torch.randn((1024, 65536), generator=g, device=cuda).half()
+    B = torch.randn((65536, 1024), generator=g, device=cuda).half()
+    bias = torch.randn((1024,), generator=g, device=cuda).half()
+    C = torch.empty((1024, 1024), dtype=torch.float16, device=cuda)
+    assert pax_b200.select_algo(A, B, C, epilogue="bias_gelu_tanh", bias=bias) == pax_b200.Algo.TC2
+    for _ in range(3):  # the two CTAs give up at different points each time
+        st = _abort_run(lambda: pax_b200.gemm(A, B, out=C, epilogue="bias_gelu_tanh", bias=bias))
+        assert st == pax_b200.Status.TIMEOUT
+        assert pax_b200.device_error() == pax_b200.Status.OK
+    del A, B
+    A2, B2 = inputs(rng, 640, 1536, 512)
+    b2 = rng.standard_normal(1536).astype(np.float16)
+    got = run_gemm(A2, B2, cuda, epi="bias_gelu_tanh", bias=b2, out_dtype=np.float16)
     check(got, oracle.gemm(A2, B2, epi="bias_gelu_tanh", bias=b2, out_dtype=np.float16), np.float16)
     assert pax_b200.device_error() == pax_b200.Status.OK
 
