@@ -594,6 +594,14 @@ def config_record(cfg_id, args, dev, flush, peak, hbm, steps, warmup):
                            "algorithmic_bytes_per_launch": alg_bytes, "traffic": traffic,
                            "traffic_over_algorithmic": traffic / alg_bytes if traffic else None}
         rec["single"] = {"us_per_gemm": r["mean"] * 1e3, "achieved": gbs, "frac": gbs / hbm}
+        # The same event pair around an empty launch (torch's one-thread
+        # spin kernel, 1 cycle), after the same L2 flush: the fixed cost an
+        # isolated, event-timed launch carries whatever the kernel does.
+        fl = timed_steps(lambda: torch.cuda._sleep(1), steps, warmup, flush, dev, 1, dev.index)
+        above = r["mean"] - fl["mean"]
+        rec["single"]["empty_launch_us"] = fl["mean"] * 1e3
+        rec["single"]["us_above_empty_launch"] = above * 1e3
+        rec["single"]["frac_above_empty_launch"] = (alg_bytes / (above * 1e-3) / 1e9 / hbm) if above > 0 else None
         rec["noalloc"] = noalloc_record(A, B, bias, C, cfg, alg_bytes, hbm, flush, dev, steps, warmup)
         rec["stream"] = decode_stream(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev)
         rec["batched"] = decode_batched(A, bias, cfg, K, N, alg_bytes, hbm, flush, dev)
@@ -625,8 +633,8 @@ def noalloc_record(A, B, bias, C, cfg, alg_bytes, hbm, flush, dev, steps, warmup
     r = timed_steps(step, steps, warmup, flush, dev, 1, dev.index)
     gbs = alg_bytes / (r["mean"] * 1e-3) / 1e9
     return {"us_per_gemm": r["mean"] * 1e3, "achieved": gbs, "frac": gbs / hbm,
-            "note": "one GEMM launch; a counter clear (cudaMemsetAsync) precedes it only in layouts that split tiles, "
-                    "which C4's lockstep layout (one CTA per 128-column tile) does not"}
+            "note": "one GEMM launch, the layout pax_gemm_ex picks, scratch in a fixed device array "
+                    "(no clearing: split-tile flags carry the launch epoch)"}
 
 
 def split_record(args, dev, flush, peak, world, rank, local, steps, warmup, gather_too):

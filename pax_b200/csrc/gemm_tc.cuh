@@ -50,6 +50,8 @@ struct TcParams {
     int tiles_m, tiles_n, num_tiles;
     int group_m;  // output tiles are visited in column-major groups of group_m tile rows
     int c_evict_first;  // store C with an L2 evict-first policy (C much larger than L2)
+    int res_tma;        // fp16 residual, fp16 C: residual chunks staged by TMA (tmR)
+    int zr;             // batched: the residual has one slice per item (else all share slice 0)
     // Work items: tiles [0, full_items) whole, then the last tail_tiles tiles
     // (the tail wave) as two column halves each, so
     // num_items = full_items + 2 * tail_tiles.
@@ -194,8 +196,8 @@ __device__ __forceinline__ TcWork tc_work(int k, const TcParams& p, const unsign
 template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
 __global__ void __launch_bounds__(64 + 32 * 8, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, const TcParams p,
-                   const __grid_constant__ TcReplicas reps) {
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
+                   const TcParams p, const __grid_constant__ TcReplicas reps) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem =
@@ -251,6 +253,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
         tma_prefetch_desc(&tmC);
+        if (p.res_tma) tma_prefetch_desc(&tmR);
     }
     if (warp == 1) {
         tmem_alloc<PAIR ? 2 : 1>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
@@ -473,8 +476,27 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         uint8_t* sbuf = sStg + (warp - 2) * Cfg::STG_BYTES;
         // C much larger than L2 passes through it once.
         const uint64_t pol_stream = l2_evict_first_policy();
+        // This warp's barrier for TMA loads into its staging buffer (residual
+        // chunks, replica reloads); every lane tracks its phase.
         const uint32_t pbar = push0 + 8u * (uint32_t)(warp - 2);
         uint32_t push_phase = 0;
+        // fp16 residual with fp16 C: each chunk's residual tile (32 rows x 64
+        // columns, the output chunk's shape) is TMA-loaded into the staging
+        // buffer, read from there and overwritten by the output chunk.  Whole
+        // 128-byte rows, each fetched once, instead of one 64-byte half-row
+        // per lane per 32-column sub-chunk.
+        constexpr bool kResSmem = RES == 1 && sizeof(OutT) == 2;
+        const bool res_tma = kResSmem && p.res_tma != 0;
+        bool res_pending = false;  // a residual load is in flight (lane 0 issued it)
+        const uint32_t sbuf_u32 = smem_u32(sbuf);
+        auto load_residual = [&](int col, int row0_, int bz_) {
+            if (lane == 0) {
+                bulk_wait_read<0>();  // the buffer's last store has read it
+                mbar_arrive_expect_tx(pbar, Cfg::STG_BYTES);
+                tma_load_3d(sbuf_u32, &tmR, pbar, col, row0_, bz_);
+            }
+            res_pending = true;
+        };
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int k = k_begin; k < k_end; k += k_step) {
@@ -493,20 +515,24 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             const long long tcol0 = (long long)wk.col0 + wcol;
             // Operands that do not depend on the accumulator are fetched before
             // waiting for it: this warp's bias and the first residual chunk.
-            const uint4 bias8 = bias_tile_load(tcol0, wcols, lane, p.N, ep);
-            ResChunk<32, RES> rc;
-            if (wcols > 0) res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, ep);
-            bool ok = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag);
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + wcol);
             // Chunks wholly outside C (beyond N, or this warp's 32 rows beyond
             // M) are neither read nor stored.
             long long valid_cols = p.N - tcol0;
             if (valid_cols > wcols) valid_cols = wcols;
             if (valid_cols < 0) valid_cols = 0;
             const int nch = row0 < p.M ? (int)((valid_cols + EC - 1) / EC) : 0;
+            const uint4 bias8 = bias_tile_load(tcol0, wcols, lane, p.N, ep);
+            ResChunk<32, RES> rc;
+            if (res_tma) {
+                if (nch > 0) load_residual((int)tcol0, row0, p.zr ? bz : 0);
+            } else if (wcols > 0) {
+                res_prefetch<32, RES>(rc, row, tcol0, p.M, p.N, ep);
+            }
+            bool ok = mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + wcol);
             auto release_accumulator = [&]() {
                 // Whole accumulator read: hand it back to the MMA warp (of the
                 // pair leader).
@@ -525,6 +551,12 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             // 32 fp32 values are live at a time.
 #pragma unroll 1
             for (int ci = 0; ci < nch; ++ci) {
+                if (res_tma) {
+                    // Every lane reads the tile, so every lane waits for it.
+                    mbar_wait(pbar, push_phase, nullptr);
+                    push_phase ^= 1u;
+                    res_pending = false;
+                }
                 uint32_t w[32];  // packed output row
 #pragma unroll
                 for (int h = 0; h < EC / 32; ++h) {
@@ -533,11 +565,20 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                     tmem_ld_32x32b_x32(t_row + (uint32_t)c, v);
                     tmem_wait_ld();
                     if (ci == nch - 1 && h == EC / 32 - 1) release_accumulator();
+                    if constexpr (kResSmem) {
+                        if (res_tma) {
+                            // This lane's row, 16-byte granules 4h..4h+3 (128B swizzle).
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                rc.u[i] = ld_shared_v4(sbuf_u32 + (uint32_t)lane * 128u +
+                                                       (uint32_t)(((4 * h + i) ^ (lane & 7)) << 4));
+                        }
+                    }
                     epi_linear<32, RES>(v, rc, bias8, c, ep);
                     // The residual registers are free again: start the next
                     // sub-chunk's loads, which then overlap the GeLU math below.
                     if constexpr (RES != 0) {
-                        if (c + 32 < nch * EC)
+                        if (!res_tma && c + 32 < nch * EC)
                             res_prefetch<32, RES>(rc, row, tcol0 + c + 32, p.M, p.N, ep);
                     }
                     epi_gelu<32, GELU>(v);
@@ -569,6 +610,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         tma_store_3d(&tmC, smem_u32(sbuf), (int)(tcol0 + ci * EC), row0, bz);
                     bulk_commit();
                 }
+                if (res_tma && ci + 1 < nch) load_residual((int)(tcol0 + (ci + 1) * EC), row0, p.zr ? bz : 0);
             }
             // Replicas: once the accumulator is handed back, this warp copies
             // its finished chunks from the local C to every replica, one chunk
@@ -592,6 +634,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         bulk_commit();
                     }
                 }
+                push_phase = __shfl_sync(0xffffffffu, push_phase, 0);  // lane 0 waited for the reloads
                 __syncwarp();
             }
             if (++acc == Cfg::ACC_BUFS) {
@@ -600,6 +643,9 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             }
         }
         if (lane == 0) {
+            // A residual load issued before an abandoned accumulator wait
+            // lands before the CTA leaves.
+            if (res_pending) mbar_wait(pbar, push_phase, nullptr);
             bulk_wait<0>();
             // Stores to other GPUs are complete; make them visible system-wide
             // before the grid ends.
@@ -685,6 +731,20 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
                    pr.batch, pr.ldc * ce, zstride(pr.batch > 1 ? pr.sc : 0, pr.M, pr.ldc * ce, ce), Cfg::EPI_COLS,
                    32))
         return PAX_ERR_CUDA;
+    // Residual tile map (fp16 residual, fp16 C, 16-byte aligned rows): same
+    // box and swizzle as C's, so a residual chunk lands where its output
+    // chunk is staged.  Otherwise tR is C's map, never read.
+    CUtensorMap tR = tC;
+    int res_tma = 0;
+    const bool zr = pr.batch > 1 && pr.sres > 0;
+    if (RES == 1 && f16 && (pr.epi.flags & EPI_RES_VEC) && (!zr || (pr.sres * 2) % 16 == 0)) {
+        res_tma = 1;
+        if (const char* e = getenv("PAX_TC_RES_TMA")) res_tma = atoi(e) != 0 ? 1 : 0;
+        if (res_tma && !make_tmap(&tR, pr.epi.residual, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, pr.N, pr.M,
+                                  zr ? pr.batch : 1, pr.epi.ld_res * 2,
+                                  zstride(zr ? pr.sres : 0, pr.M, pr.epi.ld_res * 2, 2), Cfg::EPI_COLS, 32))
+            return PAX_ERR_CUDA;
+    }
     TcReplicas reps;
     memset(&reps, 0, sizeof(reps));
     if (pr.n_replicas < 0 || pr.n_replicas > kTcMaxReplicas) return PAX_ERR_INVALID;
@@ -727,6 +787,8 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     const long long c_bytes = pr.M * pr.N * (long long)ce * pr.batch;
     p.c_evict_first = c_bytes > (64LL << 20) ? 1 : 0;
     if (const char* e = getenv("PAX_TC_C_EVICT")) p.c_evict_first = atoi(e) != 0 ? 1 : 0;
+    p.res_tma = res_tma;
+    p.zr = zr ? 1 : 0;
     p.full_items = plan.full_items;
     p.tail_tiles = plan.tail_tiles;
     p.num_items = plan.full_items + 2 * plan.tail_tiles;
@@ -751,7 +813,7 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     cfg.attrs = attr;
     cfg.numAttrs = PAIR ? 2 : 1;
     cfg.gridDim = dim3(PAIR ? 2 * plan.units : plan.units);
-    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
+    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, tR, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }
 

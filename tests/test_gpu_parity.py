@@ -685,3 +685,36 @@ def test_batched_skinny_single_launch(cuda, rng, shared, M):
         check(got[b], oracle.gemm(a, bb, epi="residual_gelu_tanh", residual=res[b], out_dtype=np.float16),
               np.float16)
         check(got2[b], oracle.gemm(a, bb, epi="bias", bias=bias[b], out_dtype=np.float32), np.float32)
+
+
+@pytest.mark.parametrize("algo", ["tc2", "wide", "256", "128"])
+def test_residual_staged_by_tma_matches_lane_loads(cuda, rng, monkeypatch, algo):
+    """fp16 residual with fp16 C: residual chunks staged in shared memory by
+    TMA give the same bits as per-lane global loads (PAX_TC_RES_TMA=0), with
+    ragged edges and a residual that is a column slice of a wider tensor."""
+    algo = _force_tile(monkeypatch, algo)
+    M, N, K = 600, 1000, 264
+    A, B = inputs(rng, M, N, K)
+    wide = rng.standard_normal((M, N + 24)).astype(np.float16)
+    tr = to_dev(wide, cuda)[:, 8:8 + N]
+    res = wide[:, 8:8 + N]
+    tA, tB = to_dev(A, cuda), to_dev(B, cuda)
+    outs = []
+    for flag in ("1", "0"):
+        monkeypatch.setenv("PAX_TC_RES_TMA", flag)
+        C = pax_b200.gemm(tA, tB, epilogue="residual_gelu_erf", residual=tr, out_dtype=torch.float16, algo=algo)
+        outs.append(C.cpu().numpy())
+    check(outs[0], oracle.gemm(A, B, epi="residual_gelu_erf", residual=res, out_dtype=np.float16), np.float16)
+    assert np.array_equal(outs[0].view(np.uint16), outs[1].view(np.uint16))
+
+
+def test_batched_shared_residual(cuda, rng):
+    """One [M, N] residual shared by every batch item (stride 0)."""
+    nb, M, N, K = 3, 384, 640, 192
+    A, B, _, res = _batched_case(rng, nb, M, N, K)
+    tA, tB, tr = to_dev(A, cuda), to_dev(B, cuda), to_dev(res[0], cuda)
+    C = pax_b200.gemm_batched(tA, tB, epilogue="residual_gelu_tanh", residual=tr, out_dtype=torch.float16)
+    got = C.cpu().numpy()
+    for b in range(nb):
+        check(got[b], oracle.gemm(A[b], B[b], epi="residual_gelu_tanh", residual=res[0], out_dtype=np.float16),
+              np.float16)
