@@ -912,6 +912,8 @@ def run_pax(args):
     # samples to say what SM clock the kernel runs at under sustained load.
     if defaults and world == 1 and not args.no_subrecords:
         sub["sustained"], _ = guarded("sustained", lambda: sustained_record(step, dev, local, flops_rank))
+        sub["same_box_comparison"], _ = guarded("same_box_comparison", lambda: comparison_record(
+            A, B, C, dev, flush, flops_rank, args.steps, max(3, args.warmup)))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -953,6 +955,21 @@ def run_pax(args):
             rc.close()
         dist.destroy_process_group()
     return 0
+
+
+def comparison_record(A, B, C, dev, flush, flops, steps, warmup):
+    """The headline shape without its epilogue, this library's kernel and
+    cuBLAS (torch.matmul, fp16), timed like the headline on the same GPU:
+    the speed of each GEMM alone, since clocks differ from box to box."""
+    import torch
+
+    import pax_b200
+
+    ours = timed_steps(lambda: pax_b200.gemm(A, B, out=C), steps, warmup, flush, dev, 1, dev.index)
+    lib = timed_steps(lambda: torch.matmul(A, B, out=C), steps, warmup, flush, dev, 1, dev.index)
+    return {"pax_no_epilogue": {"ms_per_launch": ours["mean"], "tflops": flops / (ours["mean"] * 1e-3) / 1e12},
+            "cublas_no_epilogue": {"ms_per_launch": lib["mean"], "tflops": flops / (lib["mean"] * 1e-3) / 1e12,
+                                   "how": "torch.matmul fp16 (cuBLAS), same operands, L2 flush and event timing"}}
 
 
 def sustained_record(step, dev, local, flops, seconds=0.25):
