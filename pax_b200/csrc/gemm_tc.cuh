@@ -52,6 +52,7 @@ struct TcParams {
     int c_evict_first;  // store C with an L2 evict-first policy (C much larger than L2)
     int res_tma;        // fp16 residual, fp16 C: residual chunks staged by TMA (tmR)
     int zr;             // batched: the residual has one slice per item (else all share slice 0)
+    int b_pairs;        // N % 64 == 0: B's 64-column boxes loaded two at a time (tmB2)
     // Work items: tiles [0, full_items) whole, then the last tail_tiles tiles
     // (the tail wave) as two column halves each, so
     // num_items = full_items + 2 * tail_tiles.
@@ -197,7 +198,8 @@ template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
 __global__ void __launch_bounds__(64 + 32 * 8, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
-                   const TcParams p, const __grid_constant__ TcReplicas reps) {
+                   const __grid_constant__ CUtensorMap tmB2, const TcParams p,
+                   const __grid_constant__ TcReplicas reps) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem =
@@ -254,6 +256,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         tma_prefetch_desc(&tmB);
         tma_prefetch_desc(&tmC);
         if (p.res_tma) tma_prefetch_desc(&tmR);
+        if (p.b_pairs) tma_prefetch_desc(&tmB2);
     }
     if (warp == 1) {
         tmem_alloc<PAIR ? 2 : 1>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
@@ -306,18 +309,36 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         const uint32_t fb_leader = mapa_shared(fb, 0);
                         if (leader) mbar_arrive_expect_tx(fb, 2 * bytes);
                         tma_load_3d_pair(adst, &tmA, fb_leader, kb * Cfg::BK, arow, za);
-                        // 64-column boxes: MMA 0's first, then MMA 1's.
-                        for (int j = 0; j < l0 / 64; ++j)
+                        // 64-column boxes: MMA 0's first, then MMA 1's; two
+                        // adjacent boxes in one load where B allows it.
+                        int j = 0;
+                        if (p.b_pairs)
+                            for (; j + 2 <= l0 / 64; j += 2)
+                                tma_load_4d_pair(bdst + j * 8192, &tmB2, fb_leader, 0, kb * Cfg::BK, (c0 >> 6) + j, zb);
+                        for (; j < l0 / 64; ++j)
                             tma_load_3d_pair(bdst + j * 8192, &tmB, fb_leader, c0 + j * 64, kb * Cfg::BK, zb);
-                        for (int j = 0; j < l1 / 64; ++j)
+                        j = 0;
+                        if (p.b_pairs)
+                            for (; j + 2 <= l1 / 64; j += 2)
+                                tma_load_4d_pair(bdst + (l0 / 64 + j) * 8192, &tmB2, fb_leader, 0, kb * Cfg::BK,
+                                                 (c1 >> 6) + j, zb);
+                        for (; j < l1 / 64; ++j)
                             tma_load_3d_pair(bdst + (l0 / 64 + j) * 8192, &tmB, fb_leader, c1 + j * 64, kb * Cfg::BK,
                                              zb);
                     } else {
                         mbar_arrive_expect_tx(fb, bytes);
                         tma_load_3d(adst, &tmA, fb, kb * Cfg::BK, arow, za);
-                        for (int j = 0; j < l0 / 64; ++j)
+                        int j = 0;
+                        if (p.b_pairs)
+                            for (; j + 2 <= l0 / 64; j += 2)
+                                tma_load_4d(bdst + j * 8192, &tmB2, fb, 0, kb * Cfg::BK, (c0 >> 6) + j, zb);
+                        for (; j < l0 / 64; ++j)
                             tma_load_3d(bdst + j * 8192, &tmB, fb, c0 + j * 64, kb * Cfg::BK, zb);
-                        for (int j = 0; j < l1 / 64; ++j)
+                        j = 0;
+                        if (p.b_pairs)
+                            for (; j + 2 <= l1 / 64; j += 2)
+                                tma_load_4d(bdst + (l0 / 64 + j) * 8192, &tmB2, fb, 0, kb * Cfg::BK, (c1 >> 6) + j, zb);
+                        for (; j < l1 / 64; ++j)
                             tma_load_3d(bdst + (l0 / 64 + j) * 8192, &tmB, fb, c1 + j * 64, kb * Cfg::BK, zb);
                     }
                     ++total;
@@ -731,6 +752,28 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
                    pr.batch, pr.ldc * ce, zstride(pr.batch > 1 ? pr.sc : 0, pr.M, pr.ldc * ce, ce), Cfg::EPI_COLS,
                    32))
         return PAX_ERR_CUDA;
+    // B as [batch][N/64][K][64]: two adjacent 64-column boxes per load.  Only
+    // when N is a multiple of 64, so that a box is wholly inside B or wholly
+    // outside it (zero-filled).  Otherwise tB2 is B's map, never read.
+    CUtensorMap tB2 = tB;
+    int b_pairs = 0;
+    if (pr.N % 64 == 0) {
+        b_pairs = 1;
+        if (const char* e = getenv("PAX_TC_BPAIRS")) b_pairs = atoi(e) != 0 ? 1 : 0;
+        if (b_pairs) {
+            auto enc = tensor_map_encoder();
+            cuuint64_t dims[4] = {64, (cuuint64_t)pr.K, (cuuint64_t)(pr.N / 64), (cuuint64_t)(zb ? pr.batch : 1)};
+            cuuint64_t strides[3] = {(cuuint64_t)(pr.ldb * 2), 128, (cuuint64_t)zstride(zb ? pr.sb : 0, pr.K, pr.ldb * 2, 2)};
+            cuuint32_t box[4] = {64, 64, 2, 1};
+            cuuint32_t estr[4] = {1, 1, 1, 1};
+            if (!enc || enc(&tB2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(static_cast<const void*>(pr.B)),
+                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+                tB2 = tB;
+                b_pairs = 0;
+            }
+        }
+    }
     // Residual tile map (fp16 residual, fp16 C, 16-byte aligned rows): same
     // box and swizzle as C's, so a residual chunk lands where its output
     // chunk is staged.  Otherwise tR is C's map, never read.
@@ -788,6 +831,7 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     p.c_evict_first = c_bytes > (64LL << 20) ? 1 : 0;
     if (const char* e = getenv("PAX_TC_C_EVICT")) p.c_evict_first = atoi(e) != 0 ? 1 : 0;
     p.res_tma = res_tma;
+    p.b_pairs = b_pairs;
     p.zr = zr ? 1 : 0;
     p.full_items = plan.full_items;
     p.tail_tiles = plan.tail_tiles;
@@ -813,7 +857,7 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     cfg.attrs = attr;
     cfg.numAttrs = PAIR ? 2 : 1;
     cfg.gridDim = dim3(PAIR ? 2 * plan.units : plan.units);
-    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, tR, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
+    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, tR, tB2, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }
 
