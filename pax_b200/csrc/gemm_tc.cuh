@@ -194,11 +194,24 @@ __device__ __forceinline__ TcWork tc_work(int k, const TcParams& p, const unsign
 }
 
 
+// Wide pair tile, item of width w: the accumulator column holding item
+// column ic.  CTA r stages item columns [r w/2, (r+1) w/2), the first n0/2
+// of them for MMA 0 and the rest for MMA 1; each MMA's accumulator columns
+// take CTA 0's share first, then CTA 1's.  Identity for w <= 256.
+__device__ __forceinline__ int wide_tmem_col(int ic, int w) {
+    const int n0 = w < 256 ? w : 256, h0 = n0 / 2, hw = w / 2, h1 = (w - n0) / 2;
+    if (ic < h0) return ic;
+    if (ic < hw) return n0 + (ic - h0);
+    if (ic < hw + h0) return h0 + (ic - hw);
+    return n0 + h1 + (ic - hw - h0);
+}
+
 template <int BN, int STAGES, typename OutT, int RES, int GELU, bool PAIR>
 __global__ void __launch_bounds__(64 + 32 * 8, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
-                   const __grid_constant__ CUtensorMap tmB2, const TcParams p,
+                   const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmB3,
+                   const __grid_constant__ CUtensorMap tmB4, const TcParams p,
                    const __grid_constant__ TcReplicas reps) {
     using Cfg = TcCfg<BN, STAGES, OutT, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -256,7 +269,13 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         tma_prefetch_desc(&tmB);
         tma_prefetch_desc(&tmC);
         if (p.res_tma) tma_prefetch_desc(&tmR);
-        if (p.b_pairs) tma_prefetch_desc(&tmB2);
+        if (p.b_pairs) {
+            tma_prefetch_desc(&tmB2);
+            if constexpr (Cfg::WIDE) {
+                tma_prefetch_desc(&tmB3);
+                tma_prefetch_desc(&tmB4);
+            }
+        }
     }
     if (warp == 1) {
         tmem_alloc<PAIR ? 2 : 1>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
@@ -287,12 +306,17 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             for (int k = k_begin; ok && k < k_end; k += k_step) {
                 const TcWork wk = tc_work<BN>(k, p, items);
                 const int za = p.za ? wk.bz : 0, zb = p.zb ? wk.bz : 0;
-                // MMA 0 covers item columns [0, n0), MMA 1 (items wider than
-                // 256 only) [n0, w).  This CTA stages l0 / l1 of each: half of
-                // them in pair mode (CTA r the r-th half), all of them alone.
+                // MMA 0 has N = n0, MMA 1 (items wider than 256 only) N = n1.
+                // In pair mode each CTA supplies half of each MMA's B columns
+                // (l0 / l1); alone, all of them.  Wide items: CTA r stages
+                // the item's columns [r w/2, (r+1) w/2) in one piece, its first
+                // l0 for MMA 0 and the next l1 for MMA 1, so one load can
+                // bring them all; the epilogue maps accumulator columns back
+                // to item columns (wide_tmem_col).  Otherwise CTA r stages
+                // MMA 0's columns [r l0, (r+1) l0).
                 const int n0 = wk.w < 256 ? wk.w : 256, n1 = Cfg::WIDE ? wk.w - n0 : 0;
                 const int l0 = PAIR ? n0 / 2 : n0, l1 = PAIR ? n1 / 2 : n1;
-                const int c0 = wk.col0 + (int)rank * l0, c1 = wk.col0 + n0 + (int)rank * l1;
+                const int c0 = wk.col0 + (int)rank * (l0 + l1), c1 = c0 + l0;
                 const int arow = wk.mb * Cfg::TILE_M + (int)rank * Cfg::BM;
                 const uint32_t bytes = Cfg::A_BYTES + (uint32_t)(l0 + l1) * Cfg::BK * 2;
                 for (int kb = 0; kb < num_kb; ++kb) {
@@ -309,22 +333,33 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         const uint32_t fb_leader = mapa_shared(fb, 0);
                         if (leader) mbar_arrive_expect_tx(fb, 2 * bytes);
                         tma_load_3d_pair(adst, &tmA, fb_leader, kb * Cfg::BK, arow, za);
-                        // 64-column boxes: MMA 0's first, then MMA 1's; two
-                        // adjacent boxes in one load where B allows it.
-                        int j = 0;
-                        if (p.b_pairs)
-                            for (; j + 2 <= l0 / 64; j += 2)
-                                tma_load_4d_pair(bdst + j * 8192, &tmB2, fb_leader, 0, kb * Cfg::BK, (c0 >> 6) + j, zb);
-                        for (; j < l0 / 64; ++j)
-                            tma_load_3d_pair(bdst + j * 8192, &tmB, fb_leader, c0 + j * 64, kb * Cfg::BK, zb);
-                        j = 0;
-                        if (p.b_pairs)
-                            for (; j + 2 <= l1 / 64; j += 2)
-                                tma_load_4d_pair(bdst + (l0 / 64 + j) * 8192, &tmB2, fb_leader, 0, kb * Cfg::BK,
-                                                 (c1 >> 6) + j, zb);
-                        for (; j < l1 / 64; ++j)
-                            tma_load_3d_pair(bdst + (l0 / 64 + j) * 8192, &tmB, fb_leader, c1 + j * 64, kb * Cfg::BK,
-                                             zb);
+                        // 64-column boxes: MMA 0's first, then MMA 1's; adjacent
+                        // boxes in one load where B allows it.
+                        if (Cfg::WIDE && p.b_pairs) {
+                            // This CTA's l0 + l1 columns are adjacent: 1 to 4 boxes.
+                            const int nb = (l0 + l1) / 64;
+                            const CUtensorMap* m = nb == 4 ? &tmB4 : nb == 3 ? &tmB3 : nb == 2 ? &tmB2 : nullptr;
+                            if (m != nullptr)
+                                tma_load_4d_pair(bdst, m, fb_leader, 0, kb * Cfg::BK, c0 >> 6, zb);
+                            else
+                                tma_load_3d_pair(bdst, &tmB, fb_leader, c0, kb * Cfg::BK, zb);
+                        } else {
+                            int j = 0;
+                            if (p.b_pairs)
+                                for (; j + 2 <= l0 / 64; j += 2)
+                                    tma_load_4d_pair(bdst + j * 8192, &tmB2, fb_leader, 0, kb * Cfg::BK, (c0 >> 6) + j,
+                                                     zb);
+                            for (; j < l0 / 64; ++j)
+                                tma_load_3d_pair(bdst + j * 8192, &tmB, fb_leader, c0 + j * 64, kb * Cfg::BK, zb);
+                            j = 0;
+                            if (p.b_pairs)
+                                for (; j + 2 <= l1 / 64; j += 2)
+                                    tma_load_4d_pair(bdst + (l0 / 64 + j) * 8192, &tmB2, fb_leader, 0, kb * Cfg::BK,
+                                                     (c1 >> 6) + j, zb);
+                            for (; j < l1 / 64; ++j)
+                                tma_load_3d_pair(bdst + (l0 / 64 + j) * 8192, &tmB, fb_leader, c1 + j * 64,
+                                                 kb * Cfg::BK, zb);
+                        }
                     } else {
                         mbar_arrive_expect_tx(fb, bytes);
                         tma_load_3d(adst, &tmA, fb, kb * Cfg::BK, arow, za);
@@ -553,7 +588,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + wcol);
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
             auto release_accumulator = [&]() {
                 // Whole accumulator read: hand it back to the MMA warp (of the
                 // pair leader).
@@ -583,7 +618,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                 for (int h = 0; h < EC / 32; ++h) {
                     const int c = ci * EC + 32 * h;
                     float v[32];
-                    tmem_ld_32x32b_x32(t_row + (uint32_t)c, v);
+                    tmem_ld_32x32b_x32(t_row + (uint32_t)(Cfg::WIDE ? wide_tmem_col(wcol + c, width) : wcol + c), v);
                     tmem_wait_ld();
                     if (ci == nch - 1 && h == EC / 32 - 1) release_accumulator();
                     if constexpr (kResSmem) {
@@ -755,23 +790,27 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     // B as [batch][N/64][K][64]: two adjacent 64-column boxes per load.  Only
     // when N is a multiple of 64, so that a box is wholly inside B or wholly
     // outside it (zero-filled).  Otherwise tB2 is B's map, never read.
-    CUtensorMap tB2 = tB;
+    // (The wide tile also loads 3 and 4 boxes at a time: tB3, tB4.)
+    CUtensorMap tB2 = tB, tB3 = tB, tB4 = tB;
     int b_pairs = 0;
     if (pr.N % 64 == 0) {
         b_pairs = 1;
         if (const char* e = getenv("PAX_TC_BPAIRS")) b_pairs = atoi(e) != 0 ? 1 : 0;
-        if (b_pairs) {
-            auto enc = tensor_map_encoder();
+        auto enc = tensor_map_encoder();
+        auto make_b = [&](CUtensorMap* m, uint32_t boxes) {
             cuuint64_t dims[4] = {64, (cuuint64_t)pr.K, (cuuint64_t)(pr.N / 64), (cuuint64_t)(zb ? pr.batch : 1)};
-            cuuint64_t strides[3] = {(cuuint64_t)(pr.ldb * 2), 128, (cuuint64_t)zstride(zb ? pr.sb : 0, pr.K, pr.ldb * 2, 2)};
-            cuuint32_t box[4] = {64, 64, 2, 1};
+            cuuint64_t strides[3] = {(cuuint64_t)(pr.ldb * 2), 128,
+                                     (cuuint64_t)zstride(zb ? pr.sb : 0, pr.K, pr.ldb * 2, 2)};
+            cuuint32_t box[4] = {64, 64, boxes, 1};
             cuuint32_t estr[4] = {1, 1, 1, 1};
-            if (!enc || enc(&tB2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(static_cast<const void*>(pr.B)),
-                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
-                tB2 = tB;
-                b_pairs = 0;
-            }
+            return enc != nullptr &&
+                   enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(static_cast<const void*>(pr.B)), dims,
+                       strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        };
+        if (b_pairs && !(make_b(&tB2, 2) && (!Cfg::WIDE || (make_b(&tB3, 3) && make_b(&tB4, 4))))) {
+            tB2 = tB3 = tB4 = tB;
+            b_pairs = 0;
         }
     }
     // Residual tile map (fp16 residual, fp16 C, 16-byte aligned rows): same
@@ -857,7 +896,7 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     cfg.attrs = attr;
     cfg.numAttrs = PAIR ? 2 : 1;
     cfg.gridDim = dim3(PAIR ? 2 * plan.units : plan.units);
-    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, tR, tB2, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
+    if (cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, tR, tB2, tB3, tB4, p, reps) != cudaSuccess) return PAX_ERR_CUDA;
     return cudaPeekAtLastError() == cudaSuccess ? PAX_OK : PAX_ERR_CUDA;
 }
 
