@@ -53,6 +53,7 @@ struct TcParams {
     int res_tma;        // fp16 residual, fp16 C: residual chunks staged by TMA (tmR)
     int zr;             // batched: the residual has one slice per item (else all share slice 0)
     int b_pairs;        // N % 64 == 0: B's 64-column boxes loaded two at a time (tmB2)
+    int res_evict_first;  // TMA residual loads with an L2 evict-first policy
     // Work items: tiles [0, full_items) whole, then the last tail_tiles tiles
     // (the tail wave) as two column halves each, so
     // num_items = full_items + 2 * tail_tiles.
@@ -549,7 +550,10 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             if (lane == 0) {
                 bulk_wait_read<0>();  // the buffer's last store has read it
                 mbar_arrive_expect_tx(pbar, Cfg::STG_BYTES);
-                tma_load_3d(sbuf_u32, &tmR, pbar, col, row0_, bz_);
+                if (p.res_evict_first)
+                    tma_load_3d_hint(sbuf_u32, &tmR, pbar, col, row0_, bz_, pol_stream);
+                else
+                    tma_load_3d(sbuf_u32, &tmR, pbar, col, row0_, bz_);
             }
             res_pending = true;
         };
@@ -870,6 +874,10 @@ static pax_status_t launch_tc_impl(const Problem& pr, const TcPlan& plan, cudaSt
     p.c_evict_first = c_bytes > (64LL << 20) ? 1 : 0;
     if (const char* e = getenv("PAX_TC_C_EVICT")) p.c_evict_first = atoi(e) != 0 ? 1 : 0;
     p.res_tma = res_tma;
+    // The residual is read once: with C (same size) it would otherwise push
+    // A and B out of L2.
+    p.res_evict_first = p.c_evict_first;
+    if (const char* e = getenv("PAX_TC_RES_EVICT")) p.res_evict_first = atoi(e) != 0 ? 1 : 0;
     p.b_pairs = b_pairs;
     p.zr = zr ? 1 : 0;
     p.full_items = plan.full_items;
