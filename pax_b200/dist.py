@@ -89,7 +89,7 @@ class ReplicatedC:
 
     With a `monitor` (a PeerMonitor), each call first checks on the host
     that every peer is alive and at the same step, and raises RankFailure
-    before the first all-reduce if one has left or stopped responding.
+    before the first barrier if one has left or stopped responding.
 
     `_export`, `_import`, `_close` and `gemm_fn` exist so that the host logic
     can be tested without GPUs.
@@ -198,8 +198,8 @@ class PeerMonitor:
     """Host-side failure detection between steps, through the c10d store.
 
     Ranks of a slab-partitioned job run the same steps in the same order,
-    and a step with a collective (the all-gather of C, or the ordering
-    all-reduces of `ReplicatedC`) cannot finish while a peer is missing.
+    and a step with a collective (the all-gather of C, or the barriers of
+    `ReplicatedC`) cannot finish while a peer is missing.
     Before each step's launches every rank calls `step()`:
 
     * it publishes its own step number under ``<name>/step/<rank>``;
