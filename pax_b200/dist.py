@@ -91,8 +91,8 @@ class ReplicatedC:
     that every peer is alive and at the same step, and raises RankFailure
     before the first barrier if one has left or stopped responding.
 
-    `_export`, `_import`, `_close` and `gemm_fn` exist so that the host logic
-    can be tested without GPUs.
+    `_export`, `_import`, `_close`, `_barrier` and `gemm_fn` exist so that
+    the host logic can be tested without GPUs.
     """
 
     def __init__(self, M: int, N_total: int, dtype: torch.dtype = torch.float16, device=None, group=None, *,
