@@ -259,11 +259,14 @@ class ClockSampler:
 
 class NvmlSampler:
     """SM clock, power and clock-event reasons of one GPU through NVML (the
-    library nvidia-smi reads), polled every `interval` seconds on a thread.
-    Each sample carries its host time, so `stop(window)` can keep only the
-    samples taken while the timed steps ran on the GPU.  A timed region of a
-    few milliseconds is invisible to a 50 ms nvidia-smi loop; at 2 ms it
-    gets several samples."""
+    library nvidia-smi reads), polled on a thread with `interval` seconds
+    between samples (a sample itself takes about 0.1 ms).  Each sample
+    carries its host time, so `stop(window)` can keep only the samples taken
+    while the timed steps ran on the GPU.  A timed region of a few
+    milliseconds is invisible to a 50 ms nvidia-smi loop; at 0.1 ms between
+    samples a 20-step headline region (about 5 ms with its L2 flushes) gets
+    20 or more.  The timed steps are queued on the device before the region
+    starts, so the polling thread cannot delay them."""
 
     REASONS = {  # reported name -> NVML bit (clocks_event_reasons.*)
         "hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
@@ -275,7 +278,7 @@ class NvmlSampler:
         "gpu_idle": "nvmlClocksEventReasonGpuIdle",
     }
 
-    def __init__(self, pci_bus_id: str | None = None, index: int = 0, interval: float = 0.002, nvml=None):
+    def __init__(self, pci_bus_id: str | None = None, index: int = 0, interval: float = 0.0001, nvml=None):
         if nvml is None:
             import pynvml as nvml
         self.nv = nvml
@@ -333,7 +336,7 @@ class NvmlSampler:
         return {"sm_mhz": statistics.median(s[1] for s in sel), "sm_max_mhz": self.max_mhz,
                 "reasons": sorted(n for n, b in self.bits.items() if mask & b and n != "gpu_idle"),
                 "samples": len(sel), "samples_in_window": in_window, "power_w_max": max(s[2] for s in sel),
-                "source": f"NVML every {self.interval * 1e3:.0f} ms, samples inside the timed region"}
+                "source": f"NVML, {self.interval * 1e3:g} ms between samples, samples inside the timed region"}
 
 
 def clock_sampler(dev_index: int):
