@@ -415,6 +415,16 @@ pax_status_t pax_selftest_stale_counters(cudaStream_t stream);
  * reports, and ends.  The abort path's own waits keep the 2 s limit.
  * Synchronises the device.  For tests of the failure path only. */
 pax_status_t pax_selftest_set_wait_limit(uint64_t ns);
+/* Test hook (new; no counterpart in the reference; host only, launches
+ * nothing): the work list the 256 x 512 CTA-pair tile would run for an
+ * M x N x K problem on `units` pairs, when it is planned.  Writes
+ * unit_start[0..units] and items[0..count), where item bits 0-15 are the
+ * 256-row block, 16-27 the first column / 128 and 28-29 the width (0: 512,
+ * 1: 384, 2: 256, 3: 128 columns); unit u runs items
+ * [unit_start[u], unit_start[u+1]).  Returns count, 0 when the problem is not
+ * planned (round-robin tiles), -1 on a bad argument or too small a buffer. */
+int pax_selftest_wide_plan(long long M, long long N, long long K, int units, unsigned int* items, int* unit_start,
+                           int max_items);
 
 /* Frees the device memory this library allocated on its own: the skinny
  * kernel's per-stream workspaces and the planned tile tables of the wide

@@ -338,3 +338,15 @@ int read_clear_device_error_tc() {
 }
 
 }  // namespace pax
+
+// Host-only test hook: the planned work list of the wide tile (see wide_plan).
+extern "C" int pax_selftest_wide_plan(long long M, long long N, long long K, int units, unsigned int* items,
+                                      int* unit_start, int max_items) {
+    if (M <= 0 || N <= 0 || K <= 0 || units < 1 || !items || !unit_start || max_items < 0) return -1;
+    const pax::TcItemTable* t = pax::wide_plan(M, N, K, units);
+    if (t == nullptr) return 0;
+    if (t->count > max_items) return -1;
+    for (int u = 0; u <= units; ++u) unit_start[u] = t->unit_start[u];
+    for (int i = 0; i < t->count; ++i) items[i] = t->item[i];
+    return t->count;
+}
