@@ -573,14 +573,14 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             const int row0 = mb * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
             const long long row = (long long)row0 + lane;
             const long long tcol0 = (long long)wk.col0 + wcol;
-            // Operands that do not depend on the accumulator are fetched before
-            // waiting for it: this warp's bias and the first residual chunk.
             // Chunks wholly outside C (beyond N, or this warp's 32 rows beyond
             // M) are neither read nor stored.
             long long valid_cols = p.N - tcol0;
             if (valid_cols > wcols) valid_cols = wcols;
             if (valid_cols < 0) valid_cols = 0;
             const int nch = row0 < p.M ? (int)((valid_cols + EC - 1) / EC) : 0;
+            // Operands that do not depend on the accumulator are fetched before
+            // waiting for it: this warp's bias and the first residual chunk.
             const uint4 bias8 = bias_tile_load(tcol0, wcols, lane, p.N, ep);
             ResChunk<32, RES> rc;
             if (res_tma) {
