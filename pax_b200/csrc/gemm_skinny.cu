@@ -1,18 +1,24 @@
-// gemm_skinny.cu -- swap-AB stream-K tcgen05 GEMM for small M (decode shapes).
+// gemm_skinny.cu -- swap-AB tcgen05 GEMM for small M (decode shapes).
 //
 //   C[M][N] = epi(A[M][K] . B[K][N]), M <= 64.  The reference has no separate
 //   skinny path: its kernels tile M by 128 and would leave most of every tile
 //   empty (src/rtx_gemm_epilogue.cu:362-366).  Here the product is computed
 //   transposed, C^T = B^T . A^T, so N supplies the 128-row MMA dimension and
 //   M (padded to MP, a multiple of 16) the MMA N dimension:
-//     MMA A operand: B^T tile, 128 n x 64 k, read N-major straight from B.
-//     MMA B operand: A tile, MP rows x 64 k, K-major.
-//   The work (N/128 column tiles x K/64 k-blocks) is cut into equal
-//   contiguous ranges, one per persistent CTA, so every SM streams the same
-//   number of bytes of B (stream-K).  A column tile split between CTAs is
-//   finished by whichever contributor arrives last: partial sums go to a
-//   per-CTA workspace slot and the last arriver adds them in CTA order, so the
-//   result does not depend on arrival order.
+//     MMA A operand: B^T tile, 128 n x BK k, read N-major straight from B.
+//     MMA B operand: A tile, MP rows x BK k, K-major.
+//   Two work layouts over the (column tiles x k-blocks) units:
+//     lockstep: one CTA per (tile, K slice), the slices of a tile
+//       interleaved by k-block, so all CTAs stream the same k-rows of B
+//       together (the default while tiles fit the SMs);
+//     stream-K: equal contiguous unit ranges, one per persistent CTA, each
+//       visited last to first.
+//   A column tile split between CTAs is finished by the contributor that
+//   computes its last K part: every other contributor writes its fp32
+//   partial sum to its own workspace slot and release-stores this launch's
+//   epoch into its flag; the finisher waits for those flags (bounded) and
+//   adds the partial sums in CTA order, so the result does not depend on
+//   timing and nothing needs clearing between launches.
 //
 // Warp roles as in gemm_tc.cu: warp 0 TMA, warp 1 MMA + TMEM, warps 2..5
 // epilogue.
