@@ -11,8 +11,10 @@
 // CTA layout (320 threads, one CTA per SM, or one CTA pair per two SMs with
 // tcgen05 cta_group::2; persistent over work items):
 //   warp 0      TMA producer: A 128x64 (K-major) and the item's B columns
-//               64 at a time (N-major) per k-block into a STAGES-deep ring of
-//               128B-swizzled shared-memory slots, mbarrier full/empty pairs.
+//               in 64-column boxes (N-major; up to four adjacent boxes per
+//               load when N is a multiple of 64) per k-block into a
+//               STAGES-deep ring of 128B-swizzled shared-memory slots,
+//               mbarrier full/empty pairs.
 //   warp 1      MMA issuer (the pair leader): tcgen05.mma K=16, four k-steps
 //               per stage, one MMA of N <= 256 per k-step (two for items
 //               wider than 256 columns, sharing A); commits slot releases
@@ -20,10 +22,12 @@
 //   warps 2..9  epilogue, two per TMEM lane quarter, each on half of the
 //               item's columns: tcgen05.ld 32 lanes x 32 columns, bias /
 //               residual / GeLU in registers, fp32->fp16, swizzled staging
-//               in shared memory, TMA store (and, for replicated outputs, one
-//               more TMA store per replica).  With two accumulators, buffer i
-//               is handed back to the MMA warp as soon as it is read, so the
-//               epilogue of one item overlaps the main loop of the next.
+//               in shared memory, TMA store (an fp16 residual is TMA-loaded
+//               into that staging buffer first; replicated outputs are
+//               copied to the replicas once the accumulator is handed
+//               back).  With two accumulators, buffer i is handed back to
+//               the MMA warp as soon as it is read, so the epilogue of one
+//               item overlaps the main loop of the next.
 // Work items: whole tiles and column halves of the tail wave in round-robin
 // order, or (wide tiles) a host-planned per-pair list of 512 / 384 / 256
 // column items.  Ragged M/N/K edges: TMA zero-fills out-of-range loads and
