@@ -171,36 +171,8 @@ __device__ __forceinline__ bool wait_flag(const unsigned long long* flag, unsign
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
-// 2-D tiled load global -> shared (this CTA), completion on `bar`.
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int32_t x, int32_t y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
-        : "memory");
-}
-// CTA-pair form: the load lands in this CTA's shared memory and signals the
-// mbarrier `bar` (shared::cluster address), which may be the pair leader's.
-// No multicast.
-__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                                 int32_t x, int32_t y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
-        : "memory");
-}
-// 2-D tiled store shared -> global, bulk-group completion.
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x,
-                                             int32_t y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-            reinterpret_cast<uint64_t>(map)),
-        "r"(src), "r"(x), "r"(y)
-        : "memory");
-}
-// 3-D forms (z = batch item), same completion mechanisms as the 2-D ones.
+// Tiled TMA forms with the batch item as z.  Loads complete on the mbarrier
+// `bar` (in a CTA pair, the leader's); stores complete in bulk groups.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t x,
                                             int32_t y, int32_t z) {
     asm volatile(
@@ -261,20 +233,6 @@ __device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap* map, uint32
         "r"(src), "r"(x), "r"(y), "r"(z), "l"(pol)
         : "memory");
 }
-// L2 prefetch of one 2-D box (a hint: no data reaches the SM).
-__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int32_t x, int32_t y) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(x), "r"(y)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int32_t x, int32_t y, int32_t z) {
-    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(x), "r"(y), "r"(z)
-                 : "memory");
-}
 
 // Programmatic dependent launch.  pdl_wait: block until the grid this one
 // depends on (the previous kernel in the stream, when launched with
@@ -309,12 +267,6 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile(
         "barrier.cluster.arrive.release.aligned;\n\t"
         "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Named barrier `id` over `nthreads` threads.
-template <int id, int nthreads>
-__device__ __forceinline__ void named_barrier_sync() {
-    asm volatile("bar.sync %0, %1;" ::"n"(id), "n"(nthreads) : "memory");
 }
 
 // AND of `pred` over the `nthreads` threads that meet at named barrier `id`.
